@@ -1,0 +1,439 @@
+"""Benchmark of the B200 kernels on the BASELINE configurations.
+
+Headline (the JSON line's `metric`/`value`): the BASELINE row-softmax config,
+fp16 [16384, 4096] with entries N(0, 2^2), fp32 internal math, one softmax pass
+over the whole tensor per step.  Each rank processes its own copy of that
+workload (weak scaling: the path shards by rows with no collective), so
+`value` = bytes of all ranks / max-over-ranks device time.
+
+The same line carries, under `ops`, the other BASELINE configs timed the same
+way (TFLOP/s or GB/s and the fraction of the measured peak): addmm/matmul bf16
+8192^3, attention bf16 B4 H32 S4096 D128 (non-causal and causal), conv2d fp16
+N64 C256 56x56 K256 3x3 p1, max_pool2d 3x3 s2 p1 on the conv output.
+
+`--impl reference` times the reference arm: the CPU restatement of the
+reference program (oracle/, the reference itself is Python + Triton and runs on
+CPU only through the Triton interpreter) on all host cores, on a bounded sample
+of the same workload, and prints the same metric.
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+Multi-GPU: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+"""
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+MEASURED_PEAKS = REPO / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+ROWS, COLS = 16384, 4096
+SOFTMAX_BYTES = 2 * ROWS * COLS * 2  # one fp16 read + one fp16 write per element
+SOFTMAX_BUFFERS = 4  # rotating input/output pairs: 1 GiB working set > 126 MB L2
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--ops", default="all", help="comma list of extra ops to time, 'all' or 'none'")
+    p.add_argument("--op-steps", type=int, default=10)
+    return p.parse_args()
+
+
+def load_peaks():
+    if MEASURED_PEAKS.is_file():
+        data = json.loads(MEASURED_PEAKS.read_text())
+        return {k: float(data[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(kernel: str):
+    """Per-launch DRAM bytes of `kernel` from its committed ncu summary
+    (a `traffic_bytes_per_launch: N` line in profiles/<kernel>*.md), or None."""
+    for path in sorted((REPO / "profiles").glob(f"{kernel}*.md")):
+        for line in path.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].strip()))
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------------ distributed
+class Dist:
+    def __init__(self, gpus):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.enabled = self.world > 1
+        if gpus != self.world and self.enabled:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE {self.world}")
+
+    def init(self):
+        if self.enabled:
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(
+                "nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", self.local_rank)
+            )
+
+    def barrier(self):
+        if self.enabled:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, value: float) -> float:
+        if not self.enabled:
+            return value
+        import torch.distributed as dist
+
+        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.enabled:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU while the workload runs."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device_index):
+        self.device_index = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+        except (OSError, ValueError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        samples, reasons, max_mhz = [], set(), None
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                samples.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not samples:
+            return None
+        return {"sm_mhz": statistics.median(samples), "sm_max_mhz": max_mhz, "reasons": sorted(reasons),
+                "samples": len(samples)}
+
+
+# ------------------------------------------------------------------ timing helpers
+def time_launches(fn, steps, stream):
+    """Device time (ms) of `steps` calls of fn(i) on `stream`, CUDA events."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(steps):
+        fn(i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
+def soak(fn, seconds):
+    """Runs fn back to back for about `seconds` (untimed) so that clock samples
+    cover a loaded GPU around the timed region."""
+    t0 = time.perf_counter()
+    i = 0
+    while time.perf_counter() - t0 < seconds:
+        fn(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args, dist):
+    if dist.rank != 0:
+        return
+    import oracle
+
+    threads = os.cpu_count() or 1
+    gen = torch.Generator().manual_seed(0)
+    sample_rows = 2048
+    x = (torch.randn((sample_rows, COLS), generator=gen) * 2).half()
+    x32 = oracle._f32(x)
+    for _ in range(args.warmup):
+        oracle.softmax(x32, "float16", threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.softmax(x32, "float16", threads=threads)
+    elapsed = time.perf_counter() - t0
+    bytes_per_step = 2 * sample_rows * COLS * 2
+    value = bytes_per_step * args.steps / elapsed / 1e9
+    line = {
+        "impl": "reference",
+        "metric": "softmax_fp16_16384x4096_GB/s",
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 storage, f32 math",
+        "data": "synthetic N(0, 2^2), seed 0",
+        "config": {"workload": "row softmax fp16 [16384, 4096] (BASELINE configs[1])",
+                   "sample": f"{sample_rows} of {ROWS} rows per step"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample_rows} rows x {COLS} per step, oracle/oracle.c softmax (OpenMP)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample(seconds=10.0):
+    """The oracle's softmax on a bounded sample of the workload, all host cores."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    rows = 2048
+    x = oracle._f32((torch.randn((rows, COLS), generator=torch.Generator().manual_seed(1)) * 2).half())
+    oracle.softmax(x, "float16", threads=threads)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < seconds:
+        oracle.softmax(x, "float16", threads=threads)
+        n += 1
+    elapsed = time.perf_counter() - t0
+    return {
+        "value": 2 * rows * COLS * 2 * n / elapsed / 1e9,
+        "unit": "GB/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{n} passes over {rows} of {ROWS} rows ({elapsed:.1f} s), oracle/oracle.c softmax (OpenMP)",
+    }
+
+
+# ------------------------------------------------------------------ extra ops
+def bench_ops(which, steps, dist, peaks):
+    from ninetoothed_b200 import programs
+
+    results = {}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+    gen = torch.Generator(device=dev).manual_seed(1234 + dist.rank)
+
+    def randn(*shape, dtype, scale=1.0):
+        return (torch.randn(shape, generator=gen, device=dev) * scale).to(dtype)
+
+    def record(name, fn, work, unit, peak, nsteps=steps, warm=3):
+        for i in range(warm):
+            fn(i)
+        dist.barrier()
+        ms = dist.max(time_launches(fn, nsteps, stream)) / nsteps
+        if unit == "TFLOP/s":
+            achieved = work / (ms * 1e-3) / 1e12
+        else:
+            achieved = work / (ms * 1e-3) / 1e9
+        results[name] = {"value": achieved * dist.world, "per_gpu": achieved, "unit": unit, "ms": ms,
+                         "frac": achieved / peak}
+
+    s = 8192
+    if "addmm" in which or "matmul" in which:
+        a, b, c = (randn(s, s, dtype=torch.bfloat16, scale=s ** -0.5) for _ in range(3))
+        out = torch.empty(s, s, device=dev, dtype=torch.bfloat16)
+        flops = 2.0 * s * s * s
+        if "addmm" in which:
+            record("addmm_bf16_8192", lambda i: programs.addmm_kernel(c, a, b, 1.0, 1.0, out), flops, "TFLOP/s",
+                   peaks["bf16_tflops"])
+        if "matmul" in which:
+            out16 = torch.empty(s, s, device=dev, dtype=torch.float16)
+            record("matmul_bf16_8192", lambda i: programs.matmul_kernel(a, b, out16), flops, "TFLOP/s",
+                   peaks["bf16_tflops"])
+        del a, b, c, out
+    if "attention" in which:
+        q, k, v = (randn(4, 32, 4096, 128, dtype=torch.bfloat16) for _ in range(3))
+        q = (q.float() * 128 ** -0.5).bfloat16()
+        o = torch.empty_like(q)
+        full = 4.0 * 4 * 32 * 4096 * 4096 * 128
+        record("attention_bf16_noncausal", lambda i: programs.attention_kernel(q, k, v, False, o), full, "TFLOP/s",
+               peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2)
+        record("attention_bf16_causal", lambda i: programs.attention_kernel(q, k, v, True, o), full / 2, "TFLOP/s",
+               peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2)
+        del q, k, v, o
+    if "conv2d" in which or "max_pool2d" in which:
+        xs = [randn(64, 256, 56, 56, dtype=torch.float16) for _ in range(2)]
+        w = randn(256, 256, 3, 3, dtype=torch.float16, scale=(2 / (256 * 9)) ** 0.5)
+        ys = [torch.empty(64, 256, 56, 56, device=dev, dtype=torch.float16) for _ in range(2)]
+        if "conv2d" in which:
+            flops = 2.0 * 64 * 256 * 56 * 56 * 256 * 9
+            record("conv2d_fp16_n64", lambda i: programs.conv2d_kernel(xs[i % 2], w, ys[i % 2], padding_h=1,
+                                                                       padding_w=1),
+                   flops, "TFLOP/s", peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2)
+        if "max_pool2d" in which:
+            for y in ys:
+                programs.conv2d_kernel(xs[0], w, y, padding_h=1, padding_w=1)
+            pooled = [torch.empty(64, 256, 28, 28, device=dev, dtype=torch.float16) for _ in range(2)]
+            kern = programs.max_pool2d_kernels[False]
+            nbytes = 64 * 256 * 56 * 56 * 2 + 64 * 256 * 28 * 28 * 2
+            record("max_pool2d_fp16_3x3s2p1", lambda i: kern(ys[i % 2], pooled[i % 2], WINDOW_HEIGHT=3,
+                                                             WINDOW_WIDTH=3, STRIDE_HEIGHT=2, STRIDE_WIDTH=2,
+                                                             PADDING_HEIGHT=1, PADDING_WIDTH=1),
+                   nbytes, "GB/s", peaks["hbm_gbs"])
+    return results
+
+
+# ------------------------------------------------------------------ main arm
+def run_b200(args, dist):
+    from ninetoothed_b200 import programs
+    from ninetoothed_b200.runtime import device_status
+
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    peaks, peak_kind = load_peaks()
+    stream = torch.cuda.current_stream()
+
+    gen = torch.Generator(device=dev).manual_seed(dist.rank)
+    xs = [(torch.randn((ROWS, COLS), generator=gen, device=dev) * 2).half() for _ in range(SOFTMAX_BUFFERS)]
+    ys = [torch.empty_like(x) for x in xs]
+    kernel = programs.softmax_kernel
+
+    def step(i):
+        j = i % SOFTMAX_BUFFERS
+        kernel(xs[j], ys[j], BLOCK_SIZE=COLS)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    soak(step, 1.0)
+    dist.barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = dist.max(time_launches(step, args.steps, stream))
+    dist.barrier()
+    clocks = sampler.stop()
+    ms = elapsed_ms / args.steps
+    value = SOFTMAX_BYTES * dist.world / (ms * 1e-3) / 1e9
+    achieved = SOFTMAX_BYTES / (ms * 1e-3) / 1e9  # one launch per step
+
+    # End to end through the public API: pinned host input -> device, softmax,
+    # full result -> pinned host, every step.
+    host_in = xs[0].cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step(_i):
+        x = host_in.to(dev, non_blocking=True)
+        y = programs.softmax(x)
+        host_out.copy_(y, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    dist.barrier()
+    e2e_ms = dist.max(time_launches(e2e_step, e2e_steps, stream)) / e2e_steps
+    e2e_value = SOFTMAX_BYTES * dist.world / (e2e_ms * 1e-3) / 1e9
+
+    which = set()
+    if args.ops != "none":
+        which = {"addmm", "matmul", "attention", "conv2d", "max_pool2d"} if args.ops == "all" else set(
+            args.ops.split(","))
+    ops = bench_ops(which, args.op_steps, dist, peaks) if which else {}
+    status = device_status()
+
+    cpu = cpu_baseline_sample() if (dist.rank == 0 and dist.world == 1) else None
+    if dist.rank == 0:
+        line = {
+            "metric": "softmax_fp16_16384x4096_GB/s",
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": dist.world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 storage, f32 math",
+            "data": "synthetic N(0, 2^2) generated on device per rank",
+            "config": {
+                "workload": "row softmax fp16 [16384, 4096] per GPU (BASELINE configs[1]), one launch per step",
+                "rows": ROWS, "cols": COLS, "parallelism": f"rows, dp{dist.world} (no collective)",
+                "l2": f"{SOFTMAX_BUFFERS} rotating input/output pairs (1 GiB) > 126 MB L2",
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "peak_kind": f"{peak_kind} hbm_gbs",
+                "traffic": profile_traffic("softmax"),
+                "algorithmic_bytes_per_launch": SOFTMAX_BYTES,
+            },
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": ROWS * COLS * 2,
+                    "d2h_bytes_per_step": ROWS * COLS * 2, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "device_error_word": status,
+            "ops": ops,
+            "peaks": {"kind": peak_kind, **peaks},
+        }
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, dist)
+        return 0
+    dist.init()
+    try:
+        run_b200(args, dist)
+    finally:
+        dist.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,406 @@
+// tcgen05 flash attention for the reference's exp-reduction-dot-region program
+// (tests/test_attention.py:14-70), with the application's numerics:
+//   q' = round(q * round(log2 e))            (in the input dtype)
+//   s  = q' k^T                              (fp32, tensor cores)
+//   keys >= seq_kv and (causal) keys > query masked to -inf
+//   m_new = max(m, rowmax s); p = exp2(s - m_new); alpha = exp2(m - m_new)
+//   o = o * alpha + round(p) v; l = l * alpha + rowsum p   (m = -inf, l = 1 at start)
+//   out = round(o / l)
+//
+// One CTA per (batch, head, 128-query tile); 6 warps:
+//   warp 0     TMA producer: Q once, then K_j and V_j (128 keys each) into a
+//              2-stage ring;
+//   warp 1     allocates TMEM and issues the MMAs from one thread:
+//              S_j = Q K_j^T into one of two TMEM S buffers (128 fp32 columns),
+//              O += P_j V_j into the TMEM O accumulator;
+//   warps 2-5  one thread per query row (= TMEM lane): scale Q in place, read
+//              S_j from TMEM, online softmax in registers, rescale O in TMEM
+//              when the row max moved, write P_j (rounded to the input dtype)
+//              to shared memory in the 128-byte-swizzled K-major layout the
+//              next MMA reads, and finally O / l to global memory.
+// S_{j+1} = Q K_{j+1}^T runs on the tensor cores while the softmax threads work
+// on S_j.  Causal tiles skip key blocks above the diagonal and are scheduled
+// longest first.  Every mbarrier wait is bounded in time.
+#pragma once
+
+#include <cuda.h>
+#include "common.cuh"
+#include "ptx.cuh"
+#include "gemm_tc.cuh"
+
+namespace nt {
+namespace tc {
+
+struct AttentionProblem {
+  const void *q, *k, *v;
+  void *o;
+  int64_t B, H, SQ, SK, D;
+  int64_t qsb, qsh, qss, qsd, ksb, ksh, kss, ksd, vsb, vsh, vss, vsd, osb, osh, oss, osd;
+  bool causal;
+  float log2e;
+};
+
+namespace attn {
+
+constexpr int BM = 128;  // queries per CTA
+constexpr int BN = 128;  // keys per block
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+
+template <int DP>  // head_dim padded to 64 or 128
+struct Layout {
+  static constexpr int ATOMS = DP / 64;                // 128-byte swizzle atoms along head_dim
+  static constexpr int Q_BYTES = BM * DP * 2;
+  static constexpr int KV_BYTES = BN * DP * 2;         // one K or V block
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;        // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;   // 2 stages
+  static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
+  static constexpr int CTRL_OFF = P_OFF + P_BYTES;
+  static constexpr int SMEM_BYTES = CTRL_OFF + 256 + 1024;
+};
+
+struct Params {
+  int B, H, SQ, SK, D;
+  int q_tiles;
+  int causal;
+  float log2e;
+  void *o;
+  int64_t osb, osh, oss, osd;
+};
+
+template <typename T, int DP>
+__global__ void __launch_bounds__(THREADS, 1)
+attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                 const __grid_constant__ CUtensorMap tmap_v, Params prm) {
+  using L = Layout<DP>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t ctrl = base + L::CTRL_OFF;
+  // barrier slots (8 bytes each)
+  const uint32_t q_full = ctrl + 0, q_ready = ctrl + 8;
+  auto k_full = [&](int s) { return ctrl + 16 + 8u * s; };
+  auto v_full = [&](int s) { return ctrl + 32 + 8u * s; };
+  auto kv_empty = [&](int s) { return ctrl + 48 + 8u * s; };
+  auto s_full = [&](int b) { return ctrl + 64 + 8u * b; };
+  auto s_free = [&](int b) { return ctrl + 80 + 8u * b; };
+  const uint32_t p_full = ctrl + 96, o_done = ctrl + 104;
+  volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(smem + L::CTRL_OFF + 128);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::CTRL_OFF + 132);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // Work item: heavy (late) query tiles first for causal balance.
+  const int per_head = prm.q_tiles;
+  const int bh = blockIdx.x / per_head;
+  const int qt = prm.causal ? per_head - 1 - (int)(blockIdx.x % per_head) : (int)(blockIdx.x % per_head);
+  const int b = bh / prm.H, h = bh % prm.H;
+  const int q0 = qt * BM;
+  const int kv_blocks_total = (prm.SK + BN - 1) / BN;
+  int n_blocks = kv_blocks_total;
+  if (prm.causal) n_blocks = min(n_blocks, (q0 + BM - 1) / BN + 1);
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(q_full, 1);
+    ptx::mbar_init(q_ready, 128);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(k_full(s), 1);
+      ptx::mbar_init(v_full(s), 1);
+      ptx::mbar_init(kv_empty(s), 1);
+      ptx::mbar_init(s_full(s), 1);
+      ptx::mbar_init(s_free(s), 128);
+    }
+    ptx::mbar_init(p_full, 128);
+    ptx::mbar_init(o_done, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmap_q);
+    ptx::prefetch_tmap(&tmap_k);
+    ptx::prefetch_tmap(&tmap_v);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(const_cast<uint32_t *>(tmem_base_ptr)), TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_ptr;
+  const uint32_t tmem_s0 = tmem_base, tmem_o = tmem_base + 2 * BN;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      ptx::mbar_arrive_expect_tx(q_full, L::Q_BYTES);
+      for (int a = 0; a < L::ATOMS; ++a)
+        ptx::tma_load_4d(base + L::Q_OFF + a * (BM * 128), &tmap_q, q_full, 64 * a, q0, h, b);
+      for (int j = 0; j < n_blocks; ++j) {
+        const int s = j & 1;
+        const uint32_t use = (uint32_t)(j >> 1) & 1u;
+        if (!ptx::mbar_wait(kv_empty(s), use ^ 1u, abort_flag)) break;
+        ptx::mbar_arrive_expect_tx(k_full(s), L::KV_BYTES);
+        for (int a = 0; a < L::ATOMS; ++a)
+          ptx::tma_load_4d(base + L::K_OFF + s * L::KV_BYTES + a * (BN * 128), &tmap_k, k_full(s), 64 * a, j * BN,
+                           h, b);
+        ptx::mbar_arrive_expect_tx(v_full(s), L::KV_BYTES);
+        for (int a = 0; a < L::ATOMS; ++a)
+          ptx::tma_load_4d(base + L::V_OFF + s * L::KV_BYTES + a * (BN * 128), &tmap_v, v_full(s), 64 * a, j * BN,
+                           h, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t fmt = umma_format<T>();
+      constexpr uint32_t idesc_qk = ptx::f16_idesc(fmt, 0, 0, BM, BN);   // B = K block, K-major
+      constexpr uint32_t idesc_pv = ptx::f16_idesc(fmt, 0, 1, BM, DP);   // B = V block, MN-major
+      bool ok = ptx::mbar_wait(q_ready, 0, abort_flag);
+      auto issue_qk = [&](int j) {
+        const int s = j & 1;
+        const uint32_t kb = base + L::K_OFF + s * L::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < DP / 16; ++kk) {
+          const uint32_t off = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint32_t koff = (kk / 4) * (BN * 128) + (kk % 4) * 32;
+          const uint64_t a_desc = ptx::sw128_desc(base + L::Q_OFF + off, 16, 1024);
+          const uint64_t b_desc = ptx::sw128_desc(kb + koff, 16, 1024);
+          ptx::mma_f16_ss(tmem_s0 + (uint32_t)(s * BN), a_desc, b_desc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        ptx::mma_commit(s_full(s));
+      };
+      if (ok && n_blocks > 0) {
+        ok = ptx::mbar_wait(k_full(0), 0, abort_flag);
+        if (ok) {
+          ptx::tc_fence_after();
+          issue_qk(0);
+        }
+      }
+      for (int j = 0; j < n_blocks && ok; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_blocks) {
+          const int s1 = (j + 1) & 1;
+          const uint32_t use1 = (uint32_t)((j + 1) >> 1) & 1u;
+          if (!ptx::mbar_wait(k_full(s1), use1, abort_flag)) break;
+          // S buffer s1 was last read by the softmax of block j - 1.
+          if (!ptx::mbar_wait(s_free(s1), use1 ^ 1u, abort_flag)) break;
+          ptx::tc_fence_after();
+          issue_qk(j + 1);
+        }
+        if (!ptx::mbar_wait(p_full, (uint32_t)j & 1u, abort_flag)) break;
+        if (!ptx::mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, abort_flag)) break;
+        ptx::tc_fence_after();
+        const uint32_t vb = base + L::V_OFF + s * L::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint32_t poff = (kk / 4) * (BM * 128) + (kk % 4) * 32;
+          const uint64_t a_desc = ptx::sw128_desc(base + L::P_OFF + poff, 16, 1024);
+          const uint64_t b_desc = ptx::sw128_desc(vb + kk * 16 * 128, BN * 128, 1024);
+          ptx::mma_f16_ss(tmem_o, a_desc, b_desc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(o_done);
+        ptx::mma_commit(kv_empty(s));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / correction / epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // query row within the tile = TMEM lane
+    const int qi = q0 + row;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    bool ok = ptx::mbar_wait_warp(q_full, 0, abort_flag);
+    if (ok) {
+      // q' = round(q * round(log2 e)) in place; a thread owns its row's 128-byte
+      // segment in every atom, so the swizzle does not matter.
+#pragma unroll
+      for (int a = 0; a < L::ATOMS; ++a) {
+        int4 *seg = reinterpret_cast<int4 *>(smem + L::Q_OFF + a * (BM * 128) + row * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          int4 raw = seg[c];
+          T *e = reinterpret_cast<T *>(&raw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) e[i] = from_f<T>(to_f(e[i]) * prm.log2e);
+          seg[c] = raw;
+        }
+      }
+      ptx::fence_proxy_async_smem();
+    }
+    ptx::mbar_arrive(q_ready);
+
+    float m_i = -INFINITY, l_i = 1.f;
+    for (int j = 0; j < n_blocks && ok; ++j) {
+      const int s = j & 1;
+      if (!ptx::mbar_wait_warp(s_full(s), (uint32_t)(j >> 1) & 1u, abort_flag)) { ok = false; break; }
+      ptx::tc_fence_after();
+      uint32_t sr[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        ptx::tmem_ld_32x32b_x32(tmem_s0 + lane_base + (uint32_t)(s * BN + c * 32),
+                                *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+      ptx::tmem_ld_wait();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(s_free(s));
+
+      // masks: keys past seq_kv; causal keys above the query
+      const int k0 = j * BN;
+      int limit = prm.SK - k0;  // valid keys are [0, limit)
+      if (prm.causal) limit = min(limit, qi - k0 + 1);
+      float m_blk = -INFINITY;
+      float *sv = reinterpret_cast<float *>(sr);
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        sv[c] = c < limit ? sv[c] : -INFINITY;
+        m_blk = fmaxf(m_blk, sv[c]);
+      }
+      const float m_new = fmaxf(m_i, m_blk);
+      const float alpha = exp2f(m_i - m_new);
+      float l_blk = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        sv[c] = exp2f(sv[c] - m_new);
+        l_blk += sv[c];
+      }
+      // O must hold P_{j-1} V_{j-1} before it is rescaled, and P's buffer must
+      // be free before it is rewritten.
+      if (j > 0) {
+        if (!ptx::mbar_wait_warp(o_done, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
+        ptx::tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+          for (int c = 0; c < DP / 32; ++c) {
+            uint32_t orow[32];
+            const uint32_t taddr = tmem_o + lane_base + (uint32_t)(c * 32);
+            ptx::tmem_ld_32x32b_x32(taddr, orow);
+            ptx::tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            ptx::tmem_st_32x32b_x32(taddr, orow);
+          }
+          ptx::tmem_st_wait();
+        }
+      }
+      m_i = m_new;
+      l_i = l_i * alpha + l_blk;
+      // P row -> shared memory, K-major with 128-byte swizzle: atom a holds keys
+      // [64a, 64a + 64); 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+#pragma unroll
+      for (int a = 0; a < BN / 64; ++a) {
+        uint8_t *rowp = smem + L::P_OFF + a * (BM * 128) + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          alignas(16) T pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) pk[i] = from_f<T>(sv[a * 64 + c * 8 + i]);
+          *reinterpret_cast<int4 *>(rowp + ((c ^ (row & 7)) * 16)) = *reinterpret_cast<int4 *>(pk);
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(p_full);
+    }
+
+    // epilogue: O / l -> global
+    if (ok && n_blocks > 0 && ptx::mbar_wait_warp(o_done, (uint32_t)(n_blocks - 1) & 1u, abort_flag)) {
+      ptx::tc_fence_after();
+      const float inv = 1.f / l_i;
+      T *out = static_cast<T *>(prm.o) + (int64_t)b * prm.osb + (int64_t)h * prm.osh + (int64_t)qi * prm.oss;
+      const bool row_ok = qi < prm.SQ;
+#pragma unroll 1
+      for (int c = 0; c < DP / 32; ++c) {
+        uint32_t orow[32];
+        ptx::tmem_ld_32x32b_x32(tmem_o + lane_base + (uint32_t)(c * 32), orow);
+        ptx::tmem_ld_wait();
+        if (!row_ok) continue;
+        const int d0 = c * 32;
+        const int valid = min(32, prm.D - d0);
+        if (valid <= 0) continue;
+        T *dst = out + (int64_t)d0 * prm.osd;
+        if (valid == 32 && prm.osd == 1 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            alignas(16) T pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pk[i] = from_f<T>(__uint_as_float(orow[v4 * 8 + i]) * inv);
+            *reinterpret_cast<int4 *>(dst + v4 * 8) = *reinterpret_cast<int4 *>(pk);
+          }
+        } else {
+          for (int i = 0; i < valid; ++i) dst[(int64_t)i * prm.osd] = from_f<T>(__uint_as_float(orow[i]) * inv);
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// 4-D tensor map over a [batch, heads, seq, head_dim] tensor with unit
+// head_dim stride: dims (head_dim, seq, heads, batch), box (64, 128, 1, 1),
+// 128-byte swizzle; rows past seq and columns past head_dim read as zero.
+inline bool make_tmap_bhsd(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int64_t B, int64_t H,
+                           int64_t S, int64_t D, int64_t sb, int64_t sh, int64_t ss) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)ss * 2, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace attn
+
+template <typename T>
+int try_attention(const AttentionProblem &p, cudaStream_t stream) {
+  if constexpr (sizeof(T) != 2) {
+    return kNotEligible;
+  } else {
+    using namespace attn;
+    if (p.D <= 0 || p.D > 128 || p.SK <= 0 || p.SQ <= 0) return kNotEligible;
+    const auto aligned16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if (!aligned16(p.q) || !aligned16(p.k) || !aligned16(p.v)) return kNotEligible;
+    if (p.qsd != 1 || p.ksd != 1 || p.vsd != 1) return kNotEligible;
+    for (int64_t st : {p.qsb, p.qsh, p.qss, p.ksb, p.ksh, p.kss, p.vsb, p.vsh, p.vss})
+      if ((st * 2) % 16 != 0 || st <= 0) return kNotEligible;
+    if (p.B > 65535 || p.H > 65535 || p.SQ > (1 << 30) || p.SK > (1 << 30)) return kNotEligible;
+    CUtensorMap tq, tk, tv;
+    const CUtensorMapDataType dt = tmap_dtype<T>();
+    if (!make_tmap_bhsd(&tq, p.q, dt, p.B, p.H, p.SQ, p.D, p.qsb, p.qsh, p.qss) ||
+        !make_tmap_bhsd(&tk, p.k, dt, p.B, p.H, p.SK, p.D, p.ksb, p.ksh, p.kss) ||
+        !make_tmap_bhsd(&tv, p.v, dt, p.B, p.H, p.SK, p.D, p.vsb, p.vsh, p.vss))
+      return kNotEligible;
+    Params prm;
+    prm.B = (int)p.B; prm.H = (int)p.H; prm.SQ = (int)p.SQ; prm.SK = (int)p.SK; prm.D = (int)p.D;
+    prm.q_tiles = (int)((p.SQ + BM - 1) / BM);
+    prm.causal = p.causal ? 1 : 0;
+    prm.log2e = p.log2e;
+    prm.o = p.o;
+    prm.osb = p.osb; prm.osh = p.osh; prm.oss = p.oss; prm.osd = p.osd;
+    const int64_t grid = p.B * p.H * prm.q_tiles;
+    if (grid > (1LL << 31) - 1) return kNotEligible;
+    if (p.D <= 64) {
+      auto kern = attention_kernel<T, 64>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<64>::SMEM_BYTES);
+      if (e != cudaSuccess) return (int)e;
+      kern<<<(unsigned)grid, THREADS, Layout<64>::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
+    } else {
+      auto kern = attention_kernel<T, 128>;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<128>::SMEM_BYTES);
+      if (e != cudaSuccess) return (int)e;
+      kern<<<(unsigned)grid, THREADS, Layout<128>::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
+    }
+    return launch_status();
+  }
+}
+
+}  // namespace tc
+}  // namespace nt

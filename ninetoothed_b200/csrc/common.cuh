@@ -1,0 +1,96 @@
+// Shared helpers for the sm_100a kernels of libnt_b200.so: element conversion,
+// argument checks, the device error word and the launch-error convention.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/nt_b200.h"
+
+namespace nt {
+
+// Device error word of this library (one per device, zero-initialised at load).
+// The library is a single translation unit, so this is its only definition.
+__device__ int g_error_word = 0;
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_error_word, 0, code); }
+
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr bool is_f16 = false;
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__half> {
+  static constexpr bool is_f16 = true;
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr bool is_f16 = false;
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+template <typename T> __device__ __forceinline__ float to_f(T v) { return Elem<T>::to_f(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v) { return Elem<T>::from_f(v); }
+
+// Rounds an fp32 value through float16 (the `.to(ntl.float16)` of the matmul
+// application) and returns it as fp32.
+__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+
+// The addmm application's epilogue, `beta * input + alpha * matmul_output`, with
+// Triton's typing of a scalar kernel argument against a tensor (the tensor's
+// dtype wins): beta * input is computed in the input dtype TI, alpha * the
+// float16-rounded accumulator in float16, and the sum in float16 when TI is
+// float16 (float32 when the two dtypes differ).  `beta_t` and `alpha_h` are the
+// scalars already rounded to TI and float16.  Each fp32 operation here is exact
+// or followed by one rounding to a type with at most half fp32's precision, so
+// the result is the correctly rounded value of each typed operation.
+template <typename TI>
+__device__ __forceinline__ float addmm_value(float beta_t, float alpha_h, float in, float acc) {
+  const float scaled_in = to_f(from_f<TI>(beta_t * in));
+  const float scaled_mm = round_f16(alpha_h * round_f16(acc));
+  if constexpr (sizeof(TI) == 2 && Elem<TI>::is_f16) return round_f16(scaled_in + scaled_mm);
+  return scaled_in + scaled_mm;
+}
+
+inline int launch_status() {
+  cudaError_t err = cudaGetLastError();
+  return static_cast<int>(err);
+}
+
+inline bool is_float_dtype(int dtype) {
+  return dtype == NT_B200_FLOAT16 || dtype == NT_B200_BFLOAT16 || dtype == NT_B200_FLOAT32;
+}
+
+inline bool is_half_dtype(int dtype) {
+  return dtype == NT_B200_FLOAT16 || dtype == NT_B200_BFLOAT16;
+}
+
+inline int dtype_size(int dtype) {
+  switch (dtype) {
+    case NT_B200_FLOAT16:
+    case NT_B200_BFLOAT16: return 2;
+    case NT_B200_FLOAT32: return 4;
+    default: return 0;
+  }
+}
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace nt
+
+// Dispatches `body` with `scalar_t` bound to the element type of a float dtype.
+#define NT_DISPATCH_FLOAT(dtype, ...)                                   \
+  [&]() -> int {                                                        \
+    switch (dtype) {                                                    \
+      case NT_B200_FLOAT16: { using scalar_t = __half; return __VA_ARGS__(); }        \
+      case NT_B200_BFLOAT16: { using scalar_t = __nv_bfloat16; return __VA_ARGS__(); } \
+      case NT_B200_FLOAT32: { using scalar_t = float; return __VA_ARGS__(); }         \
+      default: return NT_B200_ERR_UNSUPPORTED_DTYPE;                    \
+    }                                                                   \
+  }()

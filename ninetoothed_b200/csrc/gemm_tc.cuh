@@ -1,0 +1,355 @@
+// tcgen05 tensor-core GEMM for the reference's blocked-linalg programs:
+// matmul (tests/test_matmul.py:14-47) and addmm (tests/test_addmm.py:13-38).
+//
+// Design (one CTA per SM, persistent):
+//   warp 0      TMA producer: A tile 128x64 and B tile 64x256 per k-block into a
+//               4-stage shared-memory ring (128-byte swizzle), one mbarrier pair
+//               (full/empty) per stage;
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and
+//               issues tcgen05.mma (M=128, N=256, K=16) from one thread;
+//               tcgen05.commit releases smem stages and publishes finished
+//               accumulators;
+//   warps 2-5   epilogue: tcgen05.ld of one accumulator row per thread, the
+//               application's cast chain, 16-byte global stores; it drains one
+//               accumulator while the MMA warp fills the other.
+// Output tiles are walked in groups of 16 row-tiles so that the A and B panels
+// of a wave of 148 CTAs stay in L2.  Every mbarrier wait is bounded in time.
+#pragma once
+
+#include <cuda.h>
+#include "common.cuh"
+#include "ptx.cuh"
+
+namespace nt {
+namespace tc {
+
+constexpr int kNotEligible = -1;
+
+enum class Epilogue { kMatmul, kAddmm };
+
+struct GemmProblem {
+  const void *a, *b, *bias;
+  void *out;
+  int64_t M, N, K;
+  int64_t sam, sak, sbk, sbn, sim, sin, som, son;
+  float beta, alpha;
+};
+
+struct ConvProblem {
+  const void *input, *filter;
+  void *output;
+  int64_t n, c, h, w, k, r, s, pad_h, pad_w, P, Q;
+  int64_t is[4], fs[4], os[4];
+};
+
+// ------------------------------------------------------------------ host: tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn();
+
+// 2-D tensor map over a matrix with a contiguous inner dimension.
+inline bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                         uint64_t outer, uint64_t outer_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {outer_stride_elems * (uint64_t)elem_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T> constexpr CUtensorMapDataType tmap_dtype();
+template <> constexpr CUtensorMapDataType tmap_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
+template <> constexpr CUtensorMapDataType tmap_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
+template <> constexpr CUtensorMapDataType tmap_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+
+template <typename T> __host__ __device__ constexpr uint32_t umma_format();
+template <> __host__ __device__ constexpr uint32_t umma_format<__half>() { return 0; }
+template <> __host__ __device__ constexpr uint32_t umma_format<__nv_bfloat16>() { return 1; }
+template <> __host__ __device__ constexpr uint32_t umma_format<float>() { return 0; }
+
+// ------------------------------------------------------------------ kernel
+namespace gemm {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, GROUP_M = 16;
+constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_STAGE_BYTES = BK * BN * 2;  // 32 KB
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+
+struct Params {
+  int64_t M, N, K;
+  void *out;
+  int64_t som, son;
+  const void *bias;
+  int64_t sim, sin;
+  float beta, alpha;  // rounded to TI and float16 (addmm_value)
+  int tiles_m, tiles_n, num_kb;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int &mb, int &nb) {
+  const int per_group = GROUP_M * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(tiles_m - first_m, GROUP_M);
+  const int in_group = tile % per_group;
+  mb = first_m + in_group % gsize;
+  nb = in_group / gsize;
+}
+
+template <typename TO>
+__device__ __forceinline__ void store_row_chunk(TO *dst, const float (&v)[32], bool full, int valid) {
+  if (full) {
+    if constexpr (sizeof(TO) == 2) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        alignas(16) TO tmp[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) tmp[e] = from_f<TO>(v[i * 8 + e]);
+        *reinterpret_cast<int4 *>(dst + i * 8) = *reinterpret_cast<int4 *>(tmp);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        *reinterpret_cast<float4 *>(dst + i * 4) = make_float4(v[i * 4], v[i * 4 + 1], v[i * 4 + 2], v[i * 4 + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 32; ++e)
+      if (e < valid) dst[e] = from_f<TO>(v[e]);
+  }
+}
+
+template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, Params prm) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t a_base = base;
+  const uint32_t b_base = base + STAGES * A_STAGE_BYTES;
+  uint8_t *ctrl = smem + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES);
+  const uint32_t ctrl_addr = ptx::smem_u32(ctrl);
+  // barriers: full[S], empty[S], tfull[2], tempty[2]; then tmem base and abort flag
+  auto full_bar = [&](int s) { return ctrl_addr + 8u * s; };
+  auto empty_bar = [&](int s) { return ctrl_addr + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int b) { return ctrl_addr + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return ctrl_addr + 8u * (2 * STAGES + 2 + b); };
+  volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(ctrl + 8 * (2 * STAGES + 4));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(ctrl + 8 * (2 * STAGES + 4) + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(tfull_bar(b), 1);
+      ptx::mbar_init(tempty_bar(b), 128);
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(const_cast<uint32_t *>(tmem_base_ptr)), TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_ptr;
+
+  const int num_tiles = prm.tiles_m * prm.tiles_n;
+  const int num_kb = prm.num_kb;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t fb = full_bar(stage);
+          ptx::mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
+          const int k0 = kb * BK;
+          ptx::tma_load_2d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, k0, m0);
+          if constexpr (B_MN_MAJOR) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES + j * (BK * 128), &tmap_b, fb, n0 + 64 * j, k0);
+          } else {
+            ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES, &tmap_b, fb, k0, n0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = ptx::f16_idesc(umma_format<TI>(), 0, B_MN_MAJOR ? 1 : 0, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1) & 1u;
+        if (!ptx::mbar_wait(tempty_bar(buf), use ^ 1u, abort_flag)) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = a_base + stage * A_STAGE_BYTES;
+          const uint32_t b_addr = b_base + stage * B_STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t a_desc = ptx::sw128_desc(a_addr + kk * 32, 16, 1024);
+            uint64_t b_desc;
+            if constexpr (B_MN_MAJOR)
+              b_desc = ptx::sw128_desc(b_addr + kk * 16 * 128, BK * 128, 1024);
+            else
+              b_desc = ptx::sw128_desc(b_addr + kk * 32, 16, 1024);
+            ptx::mma_f16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::mma_commit(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) ptx::mma_commit(tfull_bar(buf));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1) & 1u;
+      if (!ptx::mbar_wait_warp(tfull_bar(buf), use, abort_flag)) break;
+      ptx::tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
+      const int64_t m = (int64_t)mb * BM + row_in_tile;
+      const int64_t n0 = (int64_t)nb * BN;
+      const bool row_ok = m < prm.M;
+      TO *out = static_cast<TO *>(prm.out);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t raw[32];
+        ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32), raw);
+        ptx::tmem_ld_wait();
+        const int64_t nc = n0 + c * 32;
+        if (!row_ok || nc >= prm.N) continue;
+        const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
+        float v[32];
+        if constexpr (EPI == Epilogue::kMatmul) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
+        } else {
+          const TI *bias = static_cast<const TI *>(prm.bias) + m * prm.sim + nc * prm.sin;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float in = e < valid ? to_f(bias[e * prm.sin]) : 0.f;
+            v[e] = addmm_value<TI>(prm.beta, prm.alpha, in, __uint_as_float(raw[e]));
+          }
+        }
+        TO *dst = out + m * prm.som + nc * prm.son;
+        const bool vec = valid == 32 && prm.son == 1 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+        if (vec || prm.son == 1) {
+          store_row_chunk<TO>(dst, v, vec, valid);
+        } else {
+          for (int e = 0; e < valid; ++e) dst[e * prm.son] = from_f<TO>(v[e]);
+        }
+      }
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(tempty_bar(buf));
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+
+// Launches the tensor-core GEMM when the operands meet its layout rules;
+// returns kNotEligible otherwise so the caller takes the general-layout path.
+template <typename TI, typename TO, Epilogue EPI>
+int try_gemm(const GemmProblem &p, cudaStream_t stream) {
+  if constexpr (sizeof(TI) != 2) {
+    return kNotEligible;
+  } else {
+    using namespace gemm;
+    if (p.K <= 0) return kNotEligible;
+    if (p.M > (1LL << 31) - 1 || p.N > (1LL << 31) - 1 || p.K > (1LL << 31) - 1) return kNotEligible;
+    // A must be K-contiguous with 16-byte aligned rows (TMA rules).
+    const auto aligned16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+    if (p.sak != 1 || (p.sam * 2) % 16 != 0 || !aligned16(p.a)) return kNotEligible;
+    if (p.M > 1 && p.sam < p.K) return kNotEligible;
+    bool b_mn;
+    if (p.sbn == 1 && (p.sbk * 2) % 16 == 0 && (p.K == 1 || p.sbk >= p.N)) b_mn = true;
+    else if (p.sbk == 1 && (p.sbn * 2) % 16 == 0 && (p.N == 1 || p.sbn >= p.K)) b_mn = false;
+    else return kNotEligible;
+    if (!aligned16(p.b)) return kNotEligible;
+    if (p.K * 2 < 16 || (!b_mn && p.K * 2 < 16) || (b_mn && p.N * 2 < 16)) return kNotEligible;
+
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, p.a, tmap_dtype<TI>(), 2, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.sam, BK, BM))
+      return kNotEligible;
+    if (b_mn) {
+      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), 2, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.sbk, 64, BK))
+        return kNotEligible;
+    } else {
+      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), 2, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.sbn, BK, BN))
+        return kNotEligible;
+    }
+    Params prm;
+    prm.M = p.M; prm.N = p.N; prm.K = p.K;
+    prm.out = p.out; prm.som = p.som; prm.son = p.son;
+    prm.bias = p.bias; prm.sim = p.sim; prm.sin = p.sin;
+    prm.beta = p.beta; prm.alpha = p.alpha;
+    prm.tiles_m = (int)((p.M + BM - 1) / BM);
+    prm.tiles_n = (int)((p.N + BN - 1) / BN);
+    prm.num_kb = (int)((p.K + BK - 1) / BK);
+    const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
+    if (tiles > (1LL << 30)) return kNotEligible;
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    auto kern = b_mn ? gemm_kernel<TI, TO, EPI, true> : gemm_kernel<TI, TO, EPI, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, prm);
+    return launch_status();
+  }
+}
+
+template <typename T>
+int try_conv(const ConvProblem &p, cudaStream_t stream) {
+  (void)p;
+  (void)stream;
+  return kNotEligible;
+}
+
+}  // namespace tc
+}  // namespace nt

@@ -1,0 +1,68 @@
+// libnt_b200.so: B200 (sm_100a) kernels for the operator programs NineToothed's
+// arrange-and-apply API generates.  The library is one translation unit so the
+// device error word is shared by every kernel without relocatable device code.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "softmax.cuh"
+#include "elementwise.cuh"
+#include "pool.cuh"
+#include "contractions.cuh"
+
+namespace nt {
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+namespace tc {
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+}  // namespace tc
+
+}  // namespace nt
+
+extern "C" int nt_b200_version(void) { return 1; }
+
+extern "C" const char *nt_b200_error_string(int code) {
+  switch (code) {
+    case 0: return "success";
+    case NT_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case NT_B200_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case NT_B200_ERR_SHAPE_MISMATCH: return "shape mismatch";
+    case NT_B200_ERR_NO_DEVICE: return "no sm_100 device";
+    case NT_B200_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    default: return cudaGetErrorString(static_cast<cudaError_t>(code));
+  }
+}
+
+extern "C" int nt_b200_device_status(void *stream, int *status) {
+  if (!status) return NT_B200_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int host = 0;
+  const int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&host, nt::g_error_word, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(nt::g_error_word, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  *status = host;
+  return 0;
+}

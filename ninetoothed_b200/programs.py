@@ -1,0 +1,371 @@
+"""The operator programs of the reference, as B200 kernel callables.
+
+Each `*_kernel` object is what `ninetoothed.make(arrangement, application,
+tensors)` returns for the corresponding reference program, with the same public
+arguments, meta keywords and return value; each plain function mirrors the
+helper the reference test wraps around it (e.g. `tests/test_matmul.py:50-61`
+`matmul(lhs, rhs)` allocates the float16 output and calls the kernel).
+
+Every call goes through `libnt_b200.so`; there is no other implementation.
+"""
+
+import random
+
+import torch
+
+from ninetoothed_b200 import _lib
+from ninetoothed_b200.runtime import (
+    FLOAT_DTYPES,
+    HALF_DTYPES,
+    Kernel,
+    KernelLaunchError,
+    ScalarArg,
+    TensorArg,
+    check_same_dtype,
+    dtype_code,
+    ptr,
+)
+
+
+def _lib_call(name, *args):
+    return getattr(_lib.library(), name)(*args)
+
+
+# --------------------------------------------------------------------- matmul
+def _launch_matmul(v, stream):
+    check_same_dtype(v, ("lhs", "rhs"))
+    lhs, rhs, out = v["lhs"], v["rhs"], v["output"]
+    m, k = lhs.shape
+    k2, n = rhs.shape
+    if k2 != k or tuple(out.shape) != (m, n):
+        raise TypeError(f"matmul shapes {tuple(lhs.shape)} @ {tuple(rhs.shape)} -> {tuple(out.shape)} disagree.")
+    return _lib_call(
+        "nt_b200_matmul", ptr(lhs), ptr(rhs), ptr(out), m, n, k, *lhs.stride(), *rhs.stride(), *out.stride(),
+        dtype_code(lhs.dtype), dtype_code(out.dtype), stream,
+    )
+
+
+# tests/test_matmul.py:14-47: arrangement(lhs, rhs, output) + application.
+matmul_kernel = Kernel(
+    name="matmul",
+    args=(TensorArg("lhs", 2, HALF_DTYPES), TensorArg("rhs", 2, HALF_DTYPES), TensorArg("output", 2)),
+    outputs=("output",),
+    launch=_launch_matmul,
+)
+
+
+def matmul(lhs, rhs):
+    """tests/test_matmul.py:50-61: float16 output of `lhs @ rhs`."""
+    output = torch.empty((lhs.shape[0], rhs.shape[1]), device=lhs.device, dtype=torch.float16)
+    return matmul_kernel(lhs, rhs, output)
+
+
+# --------------------------------------------------------------------- addmm
+def _launch_addmm(v, stream):
+    check_same_dtype(v, ("input", "mat1", "mat2"))
+    inp, a, b, out = v["input"], v["mat1"], v["mat2"], v["output"]
+    m, k = a.shape
+    k2, n = b.shape
+    if k2 != k or tuple(out.shape) != (m, n) or tuple(inp.shape) != (m, n):
+        raise TypeError("addmm shapes disagree.")
+    return _lib_call(
+        "nt_b200_addmm", ptr(inp), ptr(a), ptr(b), float(v["beta"]), float(v["alpha"]), ptr(out), m, n, k,
+        *inp.stride(), *a.stride(), *b.stride(), *out.stride(), dtype_code(a.dtype), dtype_code(out.dtype), stream,
+    )
+
+
+# tests/test_addmm.py:13-38: (input, mat1, mat2, beta, alpha, output).
+addmm_kernel = Kernel(
+    name="addmm",
+    args=(
+        TensorArg("input", 2, HALF_DTYPES),
+        TensorArg("mat1", 2, HALF_DTYPES),
+        TensorArg("mat2", 2, HALF_DTYPES),
+        ScalarArg("beta"),
+        ScalarArg("alpha"),
+        TensorArg("output", 2),
+    ),
+    outputs=("output",),
+    launch=_launch_addmm,
+)
+
+
+def addmm(input, mat1, mat2, beta=1, alpha=1, out_dtype=torch.float16):
+    """tests/test_addmm.py:41-54 (float16 output by default)."""
+    output = torch.empty((mat1.shape[0], mat2.shape[1]), device=mat1.device, dtype=out_dtype)
+    return addmm_kernel(input, mat1, mat2, beta, alpha, output)
+
+
+# --------------------------------------------------------------------- attention
+def _launch_attention(v, stream):
+    check_same_dtype(v, ("q", "k", "v", "o"))
+    q, k, vv, o = v["q"], v["k"], v["v"], v["o"]
+    b, h, sq, d = q.shape
+    if tuple(k.shape[:2]) != (b, h) or k.shape[3] != d or tuple(vv.shape) != tuple(k.shape) or o.shape != q.shape:
+        raise TypeError("attention shapes disagree.")
+    if d > 128:
+        raise TypeError("Kernel argument `q` has head dimension above the upper bound 128.")
+    qs, ks, vs, os_ = (_lib.int64_array(t.stride()) for t in (q, k, vv, o))
+    return _lib_call(
+        "nt_b200_attention", ptr(q), ptr(k), ptr(vv), int(bool(v["is_causal"])), ptr(o), b, h, sq, k.shape[2], d,
+        qs, ks, vs, os_, dtype_code(q.dtype), stream,
+    )
+
+
+# tests/test_attention.py:14-96: (q, k, v, is_causal, o), scale 1.
+attention_kernel = Kernel(
+    name="attention",
+    args=(
+        TensorArg("q", 4, HALF_DTYPES),
+        TensorArg("k", 4, HALF_DTYPES),
+        TensorArg("v", 4, HALF_DTYPES),
+        ScalarArg("is_causal"),
+        TensorArg("o", 4, HALF_DTYPES),
+    ),
+    outputs=("o",),
+    launch=_launch_attention,
+)
+
+
+def attention(q, k, v, is_causal=False):
+    """tests/test_attention.py:73-96 (softmax scale 1; callers pre-scale q)."""
+    o = torch.empty_like(q, dtype=v.dtype)
+    return attention_kernel(q, k, v, is_causal, o)
+
+
+# --------------------------------------------------------------------- conv2d
+def _launch_conv2d(v, stream):
+    check_same_dtype(v, ("input", "filter", "output"))
+    x, w, out = v["input"], v["filter"], v["output"]
+    n, c, h, wd = x.shape
+    k, c2, r, s = w.shape
+    ph, pw = int(v["padding_h"]), int(v["padding_w"])
+    p, q = h + 2 * ph - r + 1, wd + 2 * pw - s + 1
+    if c2 != c or tuple(out.shape) != (n, k, p, q):
+        raise TypeError(f"conv2d output has shape {tuple(out.shape)}; expected {(n, k, p, q)}.")
+    xs, ws, os_ = (_lib.int64_array(t.stride()) for t in (x, w, out))
+    return _lib_call(
+        "nt_b200_conv2d", ptr(x), ptr(w), ptr(out), n, c, h, wd, k, r, s, ph, pw, xs, ws, os_, dtype_code(x.dtype),
+        stream,
+    )
+
+
+# tests/test_conv2d.py:14-49 with enable_padding=True: (input, filter, output,
+# padding_h=, padding_w=).
+conv2d_kernel = Kernel(
+    name="conv2d",
+    args=(TensorArg("input", 4, HALF_DTYPES), TensorArg("filter", 4, HALF_DTYPES), TensorArg("output", 4, HALF_DTYPES)),
+    outputs=("output",),
+    launch=_launch_conv2d,
+    meta=("padding_h", "padding_w"),
+    meta_defaults={"padding_h": 0, "padding_w": 0},
+)
+
+
+def conv2d(input, filter, padding=0):
+    """tests/test_conv2d.py:90-116."""
+    if isinstance(padding, int):
+        padding = (padding, padding)
+    padding_h, padding_w = padding
+    n, _, h, w = input.shape
+    k, _, r, s = filter.shape
+    p = h + 2 * padding_h - r + 1
+    q = w + 2 * padding_w - s + 1
+    output = torch.empty((n, k, p, q), device=input.device, dtype=input.dtype)
+    return conv2d_kernel(input, filter, output, padding_h=padding_h, padding_w=padding_w)
+
+
+# --------------------------------------------------------------------- max_pool2d
+def _make_max_pool2d_launch(ceil_mode):
+    del ceil_mode  # output extents come from the output tensor
+
+    def launch(v, stream):
+        x, out = v["input"], v["output"]
+        r, s = int(v["WINDOW_HEIGHT"]), int(v["WINDOW_WIDTH"])
+        sh = int(v.get("STRIDE_HEIGHT") or r)
+        sw = int(v.get("STRIDE_WIDTH") or s)
+        ph, pw = int(v.get("PADDING_HEIGHT", 0)), int(v.get("PADDING_WIDTH", 0))
+        if x.dtype != out.dtype:
+            raise TypeError("Kernel arguments `input`, `output` must share one dtype.")
+        n, c, h, w = x.shape
+        if tuple(out.shape[:2]) != (n, c):
+            raise TypeError("max_pool2d output batch/channel extents disagree with the input.")
+        xs, os_ = _lib.int64_array(x.stride()), _lib.int64_array(out.stride())
+        return _lib_call(
+            "nt_b200_max_pool2d", ptr(x), ptr(out), n, c, h, w, xs, out.shape[2], out.shape[3], os_, r, s, sh, sw, ph,
+            pw, dtype_code(x.dtype), stream,
+        )
+
+    return launch
+
+
+def _max_pool2d_kernel(ceil_mode):
+    return Kernel(
+        name=f"max_pool2d_{'ceil' if ceil_mode else 'floor'}",
+        args=(TensorArg("input", 4), TensorArg("output", 4)),
+        outputs=("output",),
+        launch=_make_max_pool2d_launch(ceil_mode),
+        meta=("WINDOW_HEIGHT", "WINDOW_WIDTH", "STRIDE_HEIGHT", "STRIDE_WIDTH", "PADDING_HEIGHT", "PADDING_WIDTH"),
+        meta_defaults={"STRIDE_HEIGHT": 0, "STRIDE_WIDTH": 0, "PADDING_HEIGHT": 0, "PADDING_WIDTH": 0},
+    )
+
+
+# tests/test_max_pool2d.py:13-36: one kernel per ceil_mode, meta WINDOW_HEIGHT/WIDTH;
+# stride/padding keywords extend it to the padded variant (stride != window).
+max_pool2d_kernels = {ceil_mode: _max_pool2d_kernel(ceil_mode) for ceil_mode in (True, False)}
+
+
+def pooled_extent(size, window, stride, padding, ceil_mode):
+    """Output extent of a pooling window (PyTorch's rule, which the reference matches)."""
+    span = size + 2 * padding - window
+    if ceil_mode:
+        out = -(-span // stride) + 1
+        if (out - 1) * stride >= size + padding:
+            out -= 1
+        return out
+    return span // stride + 1
+
+
+def max_pool2d(input, window_shape, ceil_mode=False, stride=None, padding=0):
+    """tests/test_max_pool2d.py:39-61, plus stride/padding (defaults: stride = window, no padding)."""
+    r, s = window_shape
+    sh, sw = (stride, stride) if isinstance(stride, int) else (stride or (r, s))
+    ph, pw = (padding, padding) if isinstance(padding, int) else padding
+    n, c, h, w = input.shape
+    p = pooled_extent(h, r, sh, ph, ceil_mode)
+    q = pooled_extent(w, s, sw, pw, ceil_mode)
+    output = torch.empty(n, c, p, q, dtype=input.dtype, device=input.device)
+    return max_pool2d_kernels[ceil_mode](
+        input, output, WINDOW_HEIGHT=r, WINDOW_WIDTH=s, STRIDE_HEIGHT=sh, STRIDE_WIDTH=sw, PADDING_HEIGHT=ph,
+        PADDING_WIDTH=pw,
+    )
+
+
+# --------------------------------------------------------------------- softmax
+def _launch_softmax(v, stream):
+    x, out = v["input_row"], v["output_row"]
+    if x.dtype != out.dtype or x.shape != out.shape:
+        raise TypeError("Kernel arguments `input_row`, `output_row` must share shape and dtype.")
+    rows, cols = x.shape
+    block = v.get("BLOCK_SIZE")
+    if block is not None and int(block) != cols:
+        raise TypeError(f"BLOCK_SIZE {block} must equal the row length {cols}.")
+    return _lib_call(
+        "nt_b200_softmax", ptr(x), ptr(out), rows, cols, *x.stride(), *out.stride(), dtype_code(x.dtype), stream
+    )
+
+
+# tests/test_softmax.py:10-27: softmax_kernel(input_row, output_row, BLOCK_SIZE=cols).
+softmax_kernel = Kernel(
+    name="softmax",
+    args=(TensorArg("input_row", 2), TensorArg("output_row", 2)),
+    outputs=("output_row",),
+    launch=_launch_softmax,
+    meta=("BLOCK_SIZE",),
+    meta_defaults={"BLOCK_SIZE": None},
+)
+
+
+def softmax(input):
+    """tests/test_softmax.py:10-27."""
+    output = torch.empty_like(input)
+    return softmax_kernel(input, output, BLOCK_SIZE=input.shape[-1])
+
+
+# --------------------------------------------------------------------- elementwise
+def _launch_add(v, stream):
+    check_same_dtype(v, ("lhs", "rhs", "output"))
+    a, b, out = v["lhs"], v["rhs"], v["output"]
+    if a.shape != b.shape or a.shape != out.shape:
+        raise TypeError("add shapes disagree.")
+    return _lib_call(
+        "nt_b200_add", ptr(a), ptr(b), ptr(out), a.numel(), a.stride(0), b.stride(0), out.stride(0),
+        dtype_code(a.dtype), stream,
+    )
+
+
+add_kernel = Kernel(
+    name="add",
+    args=(TensorArg("lhs", 1), TensorArg("rhs", 1), TensorArg("output", 1)),
+    outputs=("output",),
+    launch=_launch_add,
+)
+
+
+def add(lhs, rhs):
+    """tests/test_add.py:9-24."""
+    return add_kernel(lhs, rhs, torch.empty_like(lhs))
+
+
+def _launch_pow(v, stream):
+    check_same_dtype(v, ("input", "exponent", "output"))
+    a, b, out = v["input"], v["exponent"], v["output"]
+    if a.shape != b.shape or a.shape != out.shape:
+        raise TypeError("pow shapes disagree.")
+    return _lib_call(
+        "nt_b200_pow", ptr(a), ptr(b), ptr(out), a.numel(), a.stride(0), b.stride(0), out.stride(0),
+        dtype_code(a.dtype), stream,
+    )
+
+
+pow_kernel = Kernel(
+    name="pow",
+    args=(TensorArg("input", 1), TensorArg("exponent", 1), TensorArg("output", 1)),
+    outputs=("output",),
+    launch=_launch_pow,
+)
+
+
+def pow(input, exponent):
+    """tests/test_pow.py:10-31."""
+    return pow_kernel(input, exponent, torch.empty_like(input))
+
+
+def _launch_dropout(v, stream):
+    x, out = v["input"], v["output"]
+    if x.dtype != out.dtype or x.shape != out.shape:
+        raise TypeError("Kernel arguments `input`, `output` must share shape and dtype.")
+    return _lib_call(
+        "nt_b200_dropout", ptr(x), float(v["p"]), int(v["seed"]), ptr(out), x.numel(), x.stride(0), out.stride(0),
+        dtype_code(x.dtype), stream,
+    )
+
+
+dropout_kernel = Kernel(
+    name="dropout",
+    args=(TensorArg("input", 1), ScalarArg("p"), ScalarArg("seed"), TensorArg("output", 1)),
+    outputs=("output",),
+    launch=_launch_dropout,
+)
+
+
+def dropout(input, p=0.5, seed=None):
+    """tests/test_dropout.py:20-29 (seed drawn from `random` when not given)."""
+    if seed is None:
+        seed = random.randrange(0, 2**31)
+    return dropout_kernel(input, p, seed, torch.empty_like(input))
+
+
+__all__ = [
+    "KernelLaunchError",
+    "add",
+    "add_kernel",
+    "addmm",
+    "addmm_kernel",
+    "attention",
+    "attention_kernel",
+    "conv2d",
+    "conv2d_kernel",
+    "dropout",
+    "dropout_kernel",
+    "matmul",
+    "matmul_kernel",
+    "max_pool2d",
+    "max_pool2d_kernels",
+    "pooled_extent",
+    "pow",
+    "pow_kernel",
+    "softmax",
+    "softmax_kernel",
+    "FLOAT_DTYPES",
+]

@@ -1,0 +1,336 @@
+"""Parity of the B200 kernels (through the C ABI) with the CPU oracle, the
+reference's golden outputs and the torch ops the reference tests compare with.
+
+Tolerances (written per test): bit-exact for max_pool2d, add and dropout;
+matmul/addmm/conv2d within two float16 (or bfloat16) steps of the oracle, which
+has the same fp32 products and cast chain and differs only in summation order;
+attention rtol=atol=1e-2 (bf16/fp16 outputs with fp32 statistics); softmax 1e-3
+for 16-bit outputs and torch's default allclose for fp32.
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from ninetoothed_b200 import programs
+from ninetoothed_b200.runtime import device_status
+from tests import golden_io
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _steps(ref, dtype):
+    """One rounding step of `dtype` at each |ref| (float16 or bfloat16)."""
+    r = torch.from_numpy(np.abs(ref).astype(np.float32))
+    if dtype == torch.bfloat16:
+        bits = r.to(torch.bfloat16).view(torch.int16).to(torch.int32)
+        nxt = (bits + 1).to(torch.int16).view(torch.bfloat16).float()
+        return (nxt - r.to(torch.bfloat16).float()).abs().numpy()
+    return np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
+
+
+def assert_within_steps(got, ref, dtype, steps=2, abs_sum=None):
+    """|got - ref| <= steps rounding steps of `dtype` at |ref|, plus the fp32
+    summation-order bound 2^-20 * sum_k |a_k b_k| when `abs_sum` is given (two
+    fp32 sums of the same products in different orders differ by at most a
+    few units of 2^-24 of the sum of magnitudes; near-zero results are
+    dominated by that term)."""
+    tol = steps * _steps(ref, dtype) + 1e-6
+    if abs_sum is not None:
+        tol = tol + abs_sum * 2.0 ** -20
+    err = np.abs(got - ref)
+    bad = err > tol
+    assert not bad.any(), f"{bad.sum()} elements off by more than {steps} steps; max err {err.max()}"
+
+
+@pytest.fixture(autouse=True)
+def no_device_errors():
+    yield
+    assert device_status() == 0
+
+
+# ----------------------------------------------------------------- softmax
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_softmax_baseline_config(dtype):
+    x = (torch.randn(16384, 4096) * 2).to(dtype)
+    y = programs.softmax(x.to(DEV))
+    ref = oracle.softmax(x, out_dtype=str(dtype).split(".")[-1])
+    np.testing.assert_allclose(_np(y), ref, rtol=1e-3, atol=1e-3)
+    # size-independent property: rows sum to one
+    assert torch.allclose(y.float().sum(-1), torch.ones(16384, device=DEV), atol=1e-2)
+
+
+def test_softmax_reference_test_case():
+    # tests/test_softmax.py:30-40: fp32 1823x781, torch.rand, default allclose.
+    x = torch.rand((1823, 781), device=DEV)
+    y = programs.softmax(x)
+    assert torch.allclose(y, torch.softmax(x, dim=-1))
+    np.testing.assert_allclose(_np(y), oracle.softmax(x, "float32"), rtol=1e-5, atol=1e-8)
+
+
+@pytest.mark.parametrize("shape", ((1, 1), (3, 8), (5, 4104), (7, 33000), (2, 65536)))
+def test_softmax_ragged_and_long_rows(shape):
+    x = torch.randn(shape).half()
+    y = programs.softmax(x.to(DEV))
+    np.testing.assert_allclose(_np(y), oracle.softmax(x, "float16"), rtol=1e-3, atol=1e-3)
+
+
+def test_softmax_strided_view():
+    base = torch.randn(300, 200, device=DEV).half()
+    x = base.t()  # column stride != 1
+    y = torch.empty(200, 300, device=DEV, dtype=torch.float16)
+    programs.softmax_kernel(x, y, BLOCK_SIZE=300)
+    np.testing.assert_allclose(_np(y), oracle.softmax(x.cpu(), "float16"), rtol=1e-3, atol=1e-3)
+
+
+def test_softmax_golden():
+    for name, dtype in (("softmax_f16_8x256", "float16"), ("softmax_f32_16x781", "float32")):
+        g = golden_io.load(name)
+        y = programs.softmax(golden_io.tensor(g["input"], DEV))
+        tol = 1e-3 if dtype == "float16" else 1e-5
+        np.testing.assert_allclose(_np(y), g["output"].astype(np.float32), rtol=tol, atol=tol)
+
+
+# ----------------------------------------------------------------- elementwise
+def test_add_reference_case_and_golden():
+    a, b = torch.rand(98432, device=DEV), torch.rand(98432, device=DEV)
+    assert torch.equal(programs.add(a, b), a + b)
+    g = golden_io.load("add_f32_1000")
+    out = programs.add(golden_io.tensor(g["lhs"], DEV), golden_io.tensor(g["rhs"], DEV))
+    np.testing.assert_array_equal(_np(out), g["output"])
+
+
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_add_half_odd_size_and_stride(dtype):
+    a = torch.randn(2 * 1001, device=DEV).to(dtype)[::2]
+    b = torch.randn(1001, device=DEV).to(dtype)
+    np.testing.assert_array_equal(_np(programs.add(a, b)), oracle.add(a.cpu(), b.cpu(), str(dtype).split(".")[-1]))
+
+
+def test_pow_reference_case_and_golden():
+    a, b = torch.rand(44925, device=DEV), torch.rand(44925, device=DEV)
+    assert torch.allclose(programs.pow(a, b), torch.pow(a, b), equal_nan=True)
+    g = golden_io.load("pow_f32_1000")
+    out = programs.pow(golden_io.tensor(g["input"], DEV), golden_io.tensor(g["exponent"], DEV))
+    np.testing.assert_allclose(_np(out), g["output"], rtol=1e-6)
+
+
+@pytest.mark.parametrize("name", golden_io.names("dropout_"))
+def test_dropout_golden_bit_exact(name):
+    g = golden_io.load(name)
+    x = golden_io.tensor(g["input"], DEV)
+    out = programs.dropout(x, p=float(g["p"]), seed=int(g["seed"]))
+    np.testing.assert_array_equal(_np(out), g["output"].astype(np.float32))
+
+
+def test_dropout_large_matches_oracle_and_statistics():
+    x = torch.randn(1 << 20, device=DEV).half()
+    p, seed = 0.3, 987654321
+    out = programs.dropout(x, p=p, seed=seed)
+    np.testing.assert_array_equal(_np(out), oracle.dropout(x.cpu(), p, seed, "float16"))
+    kept = (out != 0).float().mean().item()
+    assert abs(kept - (1 - p)) < 0.01
+    # tests/test_dropout.py:41-47: survivors equal x / (1 - p)
+    mask = out != 0
+    assert torch.allclose(out[mask], x[mask] / (1 - p))
+
+
+# ----------------------------------------------------------------- max_pool2d
+@pytest.mark.parametrize("ceil_mode", (False, True))
+def test_max_pool2d_reference_case(ceil_mode):
+    # tests/test_max_pool2d.py:67-83
+    x = torch.randn((32, 3, 64, 64), device=DEV).half()
+    y = programs.max_pool2d(x, (3, 3), ceil_mode=ceil_mode)
+    assert torch.equal(y, F.max_pool2d(x, (3, 3), ceil_mode=ceil_mode))
+
+
+def test_max_pool2d_baseline_config_bit_exact():
+    x = torch.randn((64, 256, 56, 56), device=DEV).half()
+    y = programs.max_pool2d(x, (3, 3), stride=2, padding=1)
+    assert torch.equal(y, F.max_pool2d(x, 3, 2, 1))
+    sample = x[:2].cpu()
+    np.testing.assert_array_equal(
+        _np(y[:2]), oracle.max_pool2d(sample, (3, 3), (28, 28), stride=(2, 2), padding=(1, 1))
+    )
+
+
+@pytest.mark.parametrize("name", golden_io.names("max_pool2d_"))
+def test_max_pool2d_golden(name):
+    g = golden_io.load(name)
+    x = golden_io.tensor(g["input"], DEV)
+    ref = g["output"]
+    out = torch.empty(ref.shape, dtype=x.dtype, device=DEV)
+    (wh, ww), (sh, sw), (ph, pw) = g["window"], g["stride"], g["padding"]
+    programs.max_pool2d_kernels[False](
+        x, out, WINDOW_HEIGHT=int(wh), WINDOW_WIDTH=int(ww), STRIDE_HEIGHT=int(sh), STRIDE_WIDTH=int(sw),
+        PADDING_HEIGHT=int(ph), PADDING_WIDTH=int(pw),
+    )
+    np.testing.assert_array_equal(_np(out), ref.astype(np.float32))
+
+
+# ----------------------------------------------------------------- matmul / addmm
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize("mnk", ((512, 512, 512), (1000, 520, 264), (128, 256, 64), (1, 256, 64), (300, 40, 24)))
+def test_matmul_against_oracle(dtype, mnk):
+    m, n, k = mnk
+    a = torch.randn((m, k)).to(dtype)
+    b = torch.randn((k, n)).to(dtype)
+    out = programs.matmul(a.to(DEV), b.to(DEV))
+    bound = oracle.matmul(a.abs(), b.abs(), "float32")
+    assert_within_steps(_np(out), oracle.matmul(a, b, "float16"), torch.float16, abs_sum=bound)
+
+
+def test_matmul_reference_case_vs_torch():
+    # tests/test_matmul.py:69-90 (fp16 512^3); fp32-accumulated results agree
+    # with torch.matmul to float16 rounding.
+    a = torch.randn((512, 512), device=DEV).half()
+    b = torch.randn((512, 512), device=DEV).half()
+    assert torch.allclose(programs.matmul(a, b), torch.matmul(a, b), rtol=1e-2, atol=1e-2)
+
+
+def test_matmul_transposed_rhs_and_strided_output():
+    a = torch.randn((256, 192), device=DEV).half()
+    bt = torch.randn((320, 192), device=DEV).half()
+    b = bt.t()  # K-contiguous rhs
+    out = torch.empty((256, 640), device=DEV, dtype=torch.float16)[:, ::2]
+    programs.matmul_kernel(a, b, out)
+    bound = oracle.matmul(a.cpu().abs(), b.cpu().abs(), "float32")
+    assert_within_steps(_np(out), oracle.matmul(a.cpu(), b.cpu(), "float16"), torch.float16, abs_sum=bound)
+
+
+@pytest.mark.parametrize("out_dtype", (torch.bfloat16, torch.float32))
+def test_matmul_output_dtypes(out_dtype):
+    a = torch.randn((384, 128)).bfloat16()
+    b = torch.randn((128, 512)).bfloat16()
+    out = torch.empty((384, 512), device=DEV, dtype=out_dtype)
+    programs.matmul_kernel(a.to(DEV), b.to(DEV), out)
+    ref = oracle.matmul(a, b, str(out_dtype).split(".")[-1])
+    bound = oracle.matmul(a.abs(), b.abs(), "float32")
+    steps_dtype = torch.bfloat16 if out_dtype == torch.bfloat16 else torch.float16
+    assert_within_steps(_np(out), ref, steps_dtype, abs_sum=bound)
+
+
+@pytest.mark.parametrize("name", golden_io.names("matmul_f16"))
+def test_matmul_golden(name):
+    g = golden_io.load(name)
+    out = programs.matmul(golden_io.tensor(g["lhs"], DEV), golden_io.tensor(g["rhs"], DEV))
+    bound = oracle.matmul(np.abs(g["lhs"].astype(np.float32)), np.abs(g["rhs"].astype(np.float32)), "float32")
+    assert_within_steps(_np(out), g["output"].astype(np.float32), torch.float16, abs_sum=bound)
+
+
+def test_addmm_reference_case():
+    # tests/test_addmm.py:57-90: fp16 512^3, beta, alpha ~ U(0, 1), atol 0.075.
+    inp, a, b = (torch.randn((512, 512), device=DEV).half() for _ in range(3))
+    beta, alpha = 0.37, 0.81
+    out = programs.addmm(inp, a, b, beta=beta, alpha=alpha)
+    assert torch.allclose(out, torch.addmm(inp, a, b, beta=beta, alpha=alpha), atol=0.075)
+    ref = oracle.addmm(inp.cpu(), a.cpu(), b.cpu(), beta, alpha, "float16")
+    bound = alpha * oracle.matmul(a.cpu().abs(), b.cpu().abs(), "float32")
+    assert_within_steps(_np(out), ref, torch.float16, abs_sum=bound)
+
+
+def test_addmm_golden():
+    g = golden_io.load("addmm_f16_48x64x80")
+    t = {k: golden_io.tensor(g[k], DEV) for k in ("input", "mat1", "mat2")}
+    out = programs.addmm(t["input"], t["mat1"], t["mat2"], beta=float(g["beta"]), alpha=float(g["alpha"]))
+    bound = oracle.matmul(np.abs(g["mat1"].astype(np.float32)), np.abs(g["mat2"].astype(np.float32)), "float32")
+    assert_within_steps(_np(out), g["output"].astype(np.float32), torch.float16, abs_sum=bound)
+
+
+def test_addmm_baseline_config_sampled_rows():
+    # BASELINE addmm: bf16 8192^3, N(0,1)/sqrt(8192), beta = alpha = 1, bf16 out.
+    gen = torch.Generator().manual_seed(3)
+    s = 8192 ** -0.5
+    inp, a, b = ((torch.randn((8192, 8192), generator=gen) * s).bfloat16() for _ in range(3))
+    out = programs.addmm(inp.to(DEV), a.to(DEV), b.to(DEV), beta=1.0, alpha=1.0, out_dtype=torch.bfloat16)
+    rows = torch.tensor([0, 1, 127, 128, 4095, 8191])
+    ref = oracle.addmm(inp[rows], a[rows], b, 1.0, 1.0, "bfloat16")
+    bound = oracle.matmul(a[rows].abs(), b.abs(), "float32")
+    assert_within_steps(_np(out[rows.to(DEV)]), ref, torch.bfloat16, abs_sum=bound)
+
+
+# ----------------------------------------------------------------- attention
+@pytest.mark.parametrize("is_causal", (False, True))
+@pytest.mark.parametrize("seq_len", (1024, 1))
+def test_attention_reference_case(seq_len, is_causal):
+    # tests/test_attention.py:99-117: B2 H4 D64 fp16, vs sdpa(scale=1), rtol=atol=1e-2.
+    q, k, v = (torch.randn(2, 4, seq_len, 64, device=DEV).half() for _ in range(3))
+    o = programs.attention(q, k, v, is_causal=is_causal)
+    expected = F.scaled_dot_product_attention(q, k, v, is_causal=is_causal, scale=1)
+    assert torch.allclose(o, expected, rtol=1e-2, atol=1e-2)
+    ref = oracle.attention(q.cpu(), k.cpu(), v.cpu(), is_causal, "float16", block_n=64)
+    np.testing.assert_allclose(_np(o), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("name", golden_io.names("attention_"))
+def test_attention_golden(name):
+    g = golden_io.load(name)
+    q, k, v = (golden_io.tensor(g[x], DEV) for x in ("q", "k", "v"))
+    o = programs.attention(q, k, v, is_causal=bool(g["is_causal"]))
+    np.testing.assert_allclose(_np(o), g["o"].astype(np.float32), rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("is_causal", (False, True))
+def test_attention_baseline_config_sampled_heads(is_causal):
+    # BASELINE: bf16 B4 H32 S4096 D128, scale 1/sqrt(128) by pre-scaling q.
+    gen = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(4, 32, 4096, 128, generator=gen).bfloat16() for _ in range(3))
+    q = (q * 128 ** -0.5).bfloat16()
+    o = programs.attention(q.to(DEV), k.to(DEV), v.to(DEV), is_causal=is_causal)
+    sel = (slice(0, 1), slice(0, 2))
+    ref = oracle.attention(q[sel], k[sel], v[sel], is_causal, "bfloat16", block_n=64)
+    np.testing.assert_allclose(_np(o[sel]), ref, rtol=1e-2, atol=1e-2)
+
+
+def test_attention_ragged_seq_and_head_dim():
+    q = torch.randn(1, 3, 200, 96, device=DEV).half()
+    k = torch.randn(1, 3, 333, 96, device=DEV).half()
+    v = torch.randn(1, 3, 333, 96, device=DEV).half()
+    for causal in (False, True):
+        o = programs.attention(q, k, v, is_causal=causal)
+        ref = oracle.attention(q.cpu(), k.cpu(), v.cpu(), causal, "float16", block_n=64)
+        np.testing.assert_allclose(_np(o), ref, rtol=1e-2, atol=1e-2)
+
+
+# ----------------------------------------------------------------- conv2d
+@pytest.mark.parametrize("padding", (0, (1, 1), (0, 1), (2, 0)))
+def test_conv2d_reference_case(padding):
+    # tests/test_conv2d.py:119-136: N4 C64 16x16 K512 3x3, torch.rand, rtol=atol=1e-3.
+    x = torch.rand((4, 64, 16, 16), device=DEV).half()
+    w = torch.rand((512, 64, 3, 3), device=DEV).half()
+    y = programs.conv2d(x, w, padding=padding)
+    assert torch.allclose(y, F.conv2d(x, w, padding=padding), rtol=1e-3, atol=1e-3)
+    pad = (padding, padding) if isinstance(padding, int) else padding
+    bound = oracle.conv2d(x.cpu().abs(), w.cpu().abs(), pad, "float32")
+    assert_within_steps(_np(y), oracle.conv2d(x.cpu(), w.cpu(), pad, "float16"), torch.float16, abs_sum=bound)
+
+
+@pytest.mark.parametrize("name", golden_io.names("conv2d_"))
+def test_conv2d_golden(name):
+    g = golden_io.load(name)
+    x, w = golden_io.tensor(g["input"], DEV), golden_io.tensor(g["filter"], DEV)
+    pad = tuple(int(p) for p in g["padding"])
+    y = programs.conv2d(x, w, padding=pad)
+    bound = oracle.conv2d(np.abs(g["input"].astype(np.float32)), np.abs(g["filter"].astype(np.float32)), pad,
+                          "float32")
+    assert_within_steps(_np(y), g["output"].astype(np.float32), torch.float16, abs_sum=bound)
+
+
+def test_conv2d_baseline_config_sampled_images():
+    # BASELINE conv: fp16 N64 C256 56x56 K256 3x3 pad 1.
+    gen = torch.Generator().manual_seed(7)
+    x = torch.randn((64, 256, 56, 56), generator=gen).half()
+    w = (torch.randn((256, 256, 3, 3), generator=gen) * (2 / (256 * 9)) ** 0.5).half()
+    y = programs.conv2d(x.to(DEV), w.to(DEV), padding=1)
+    for sl in (slice(0, 1), slice(63, 64)):
+        ref = oracle.conv2d(x[sl], w, (1, 1), "float16")
+        bound = oracle.conv2d(x[sl].abs(), w.abs(), (1, 1), "float32")
+        assert_within_steps(_np(y[sl]), ref, torch.float16, abs_sum=bound)
