@@ -41,6 +41,9 @@ SOFTMAX_BYTES = 2 * ROWS * COLS * 2  # one fp16 read + one fp16 write per elemen
 SOFTMAX_BUFFERS = 4  # rotating input/output pairs: 1 GiB working set > 126 MB L2
 
 
+SINGLE_OPS = ("softmax", "matmul", "addmm", "attention", "attention_causal", "conv2d", "max_pool2d")
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -49,6 +52,11 @@ def parse_args():
     p.add_argument("--impl", choices=("b200", "reference"), default="b200")
     p.add_argument("--ops", default="all", help="comma list of extra ops to time, 'all' or 'none'")
     p.add_argument("--op-steps", type=int, default=10)
+    p.add_argument("--soak-seconds", type=float, default=1.0,
+                   help="untimed back-to-back steps before the timed region (clock samples cover both)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="duration of the CPU-baseline sample")
+    p.add_argument("--only", default=None, choices=sorted(SINGLE_OPS),
+                   help="run W + K launches of one op on its BASELINE shape (for profiling) and exit")
     return p.parse_args()
 
 
@@ -324,6 +332,60 @@ def bench_ops(which, steps, dist, peaks):
     return results
 
 
+# ------------------------------------------------------------------ single-op mode
+def run_single(args):
+    """W + K launches of one op on its BASELINE shape, device-timed; prints one
+    JSON line.  Used for ncu captures (`ncu ... python bench.py --only OP`)."""
+    from ninetoothed_b200 import programs
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def randn(*shape, dtype, scale=1.0):
+        return (torch.randn(shape, generator=gen, device=dev) * scale).to(dtype)
+
+    op = args.only
+    if op == "softmax":
+        x = randn(ROWS, COLS, dtype=torch.float16, scale=2.0)
+        y = torch.empty_like(x)
+        fn = lambda: programs.softmax_kernel(x, y, BLOCK_SIZE=COLS)  # noqa: E731
+        work, unit = SOFTMAX_BYTES, "GB/s"
+    elif op in ("matmul", "addmm"):
+        s = 8192
+        a, b, c = (randn(s, s, dtype=torch.bfloat16, scale=s ** -0.5) for _ in range(3))
+        out = torch.empty(s, s, device=dev, dtype=torch.bfloat16 if op == "addmm" else torch.float16)
+        if op == "addmm":
+            fn = lambda: programs.addmm_kernel(c, a, b, 1.0, 1.0, out)  # noqa: E731
+        else:
+            fn = lambda: programs.matmul_kernel(a, b, out)  # noqa: E731
+        work, unit = 2.0 * s ** 3, "TFLOP/s"
+    elif op.startswith("attention"):
+        causal = op == "attention_causal"
+        q, k, v = (randn(4, 32, 4096, 128, dtype=torch.bfloat16) for _ in range(3))
+        o = torch.empty_like(q)
+        fn = lambda: programs.attention_kernel(q, k, v, causal, o)  # noqa: E731
+        work, unit = 4.0 * 4 * 32 * 4096 * 4096 * 128 / (2 if causal else 1), "TFLOP/s"
+    elif op == "conv2d":
+        x = randn(64, 256, 56, 56, dtype=torch.float16)
+        w = randn(256, 256, 3, 3, dtype=torch.float16, scale=(2 / (256 * 9)) ** 0.5)
+        y = torch.empty(64, 256, 56, 56, device=dev, dtype=torch.float16)
+        fn = lambda: programs.conv2d_kernel(x, w, y, padding_h=1, padding_w=1)  # noqa: E731
+        work, unit = 2.0 * 64 * 256 * 56 * 56 * 256 * 9, "TFLOP/s"
+    else:
+        x = randn(64, 256, 56, 56, dtype=torch.float16)
+        y = torch.empty(64, 256, 28, 28, device=dev, dtype=torch.float16)
+        kern = programs.max_pool2d_kernels[False]
+        fn = lambda: kern(x, y, WINDOW_HEIGHT=3, WINDOW_WIDTH=3, STRIDE_HEIGHT=2, STRIDE_WIDTH=2,  # noqa: E731
+                          PADDING_HEIGHT=1, PADDING_WIDTH=1)
+        work, unit = 64 * 256 * 56 * 56 * 2 + 64 * 256 * 28 * 28 * 2, "GB/s"
+    for _ in range(args.warmup):
+        fn()
+    ms = time_launches(lambda i: fn(), args.steps, torch.cuda.current_stream()) / max(args.steps, 1)
+    rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
+    print(json.dumps({"only": op, "ms": ms, "value": rate, "unit": unit, "launches": args.warmup + args.steps}))
+
+
 # ------------------------------------------------------------------ main arm
 def run_b200(args, dist):
     from ninetoothed_b200 import programs
@@ -349,7 +411,7 @@ def run_b200(args, dist):
 
     sampler = ClockSampler(dev.index)
     sampler.start()
-    soak(step, 1.0)
+    soak(step, args.soak_seconds)
     dist.barrier()
     torch.cuda.synchronize()
     elapsed_ms = dist.max(time_launches(step, args.steps, stream))
@@ -383,7 +445,7 @@ def run_b200(args, dist):
     ops = bench_ops(which, args.op_steps, dist, peaks) if which else {}
     status = device_status()
 
-    cpu = cpu_baseline_sample() if (dist.rank == 0 and dist.world == 1) else None
+    cpu = cpu_baseline_sample(args.cpu_seconds) if (dist.rank == 0 and dist.world == 1) else None
     if dist.rank == 0:
         line = {
             "metric": "softmax_fp16_16384x4096_GB/s",
@@ -423,6 +485,9 @@ def run_b200(args, dist):
 
 def main():
     args = parse_args()
+    if args.only:
+        run_single(args)
+        return 0
     dist = Dist(args.gpus)
     if args.impl == "reference":
         run_reference(args, dist)

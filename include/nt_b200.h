@@ -137,10 +137,12 @@ int nt_b200_matmul(const void *lhs, const void *rhs, void *output, int64_t m,
                    void *stream);
 
 /*
- * output = beta * input + alpha * cast_f16(mat1 @ mat2) in fp32, stored in
- * out_dtype: the `addmm` application (tests/test_addmm.py:13-38), whose inlined
- * matmul rounds the accumulator to float16 before the epilogue.  `input` has the
- * output's [M,N] shape and in_dtype.
+ * output = beta * input + alpha * cast_f16(mat1 @ mat2), stored in out_dtype:
+ * the `addmm` application (tests/test_addmm.py:13-38), whose inlined matmul
+ * rounds the fp32 accumulator to float16.  The epilogue follows Triton's typing
+ * of a scalar argument against a tensor: beta * input in in_dtype, alpha * the
+ * float16 product in float16, their sum in float16 when in_dtype is FLOAT16
+ * (fp32 otherwise).  `input` has the output's [M,N] shape and in_dtype.
  */
 int nt_b200_addmm(const void *input, const void *mat1, const void *mat2, float beta,
                   float alpha, void *output, int64_t m, int64_t n, int64_t k,
@@ -171,12 +173,25 @@ int nt_b200_attention(const void *q, const void *k, const void *v, int is_causal
  * input[n,c,p+r-pad_h,q+s-pad_w] * filter[k,c,r,s])), zero outside the input,
  * stride 1, fp32 accumulation.  NCHW input/output, KCRS filter; strides are
  * 4-entry element-stride arrays.  dtype: FLOAT16 or BFLOAT16 (all three tensors).
+ *
+ * `workspace` is caller-owned device memory of at least
+ * nt_b200_conv2d_workspace_size(...) bytes, 256-byte aligned; the tensor-core
+ * path stages the input as NHWC and the filter as KRSC there.  With a smaller
+ * (or null) workspace the call takes the CUDA-core path instead.
  */
 int nt_b200_conv2d(const void *input, const void *filter, void *output, int64_t n,
                    int64_t c, int64_t h, int64_t w, int64_t k, int64_t r, int64_t s,
                    int64_t pad_h, int64_t pad_w, const int64_t *input_strides,
                    const int64_t *filter_strides, const int64_t *output_strides,
-                   int dtype, void *stream);
+                   void *workspace, int64_t workspace_bytes, int dtype, void *stream);
+
+/*
+ * Workspace bytes the tensor-core conv2d path needs for this problem (0 when
+ * the path does not apply: 32-bit dtype or channels not a multiple of 8).
+ * No counterpart in the reference (its conv2d program stages nothing).
+ */
+int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w,
+                                      int64_t k, int64_t r, int64_t s, int dtype);
 
 #ifdef __cplusplus
 }

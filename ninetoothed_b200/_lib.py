@@ -74,8 +74,9 @@ SIGNATURES = {
     ),
     "nt_b200_conv2d": (
         ctypes.c_int,
-        (_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _PI64, _PI64, _PI64, _C, _P),
+        (_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _PI64, _PI64, _PI64, _P, _I, _C, _P),
     ),
+    "nt_b200_conv2d_workspace_size": (ctypes.c_int64, (_I, _I, _I, _I, _I, _I, _I, _C)),
 }
 
 _lock = threading.Lock()

@@ -106,7 +106,8 @@ extern "C" int nt_b200_addmm(const void *input, const void *mat1, const void *ma
 extern "C" int nt_b200_conv2d(const void *input, const void *filter, void *output, int64_t n, int64_t c, int64_t h,
                               int64_t w, int64_t k, int64_t r, int64_t s, int64_t pad_h, int64_t pad_w,
                               const int64_t *input_strides, const int64_t *filter_strides,
-                              const int64_t *output_strides, int dtype, void *stream) {
+                              const int64_t *output_strides, void *workspace, int64_t workspace_bytes, int dtype,
+                              void *stream) {
   if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0 || pad_h < 0 || pad_w < 0)
     return NT_B200_ERR_INVALID_ARGUMENT;
   if (!nt::is_half_dtype(dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
@@ -122,7 +123,7 @@ extern "C" int nt_b200_conv2d(const void *input, const void *filter, void *outpu
     const nt::tc::ConvProblem prob{input, filter, output, n, c, h, w, k, r, s, pad_h, pad_w, P, Q,
                                    {is[0], is[1], is[2], is[3]}, {fs[0], fs[1], fs[2], fs[3]},
                                    {os[0], os[1], os[2], os[3]}};
-    const int rc = nt::tc::try_conv<T>(prob, st);
+    const int rc = nt::tc::try_conv<T>(prob, workspace, workspace_bytes, st);
     if (rc != nt::tc::kNotEligible) return rc;
     nt::simt::Im2col<T> A{static_cast<const T *>(input), c, h, w, r, s, P, Q, pad_h, pad_w,
                           is[0], is[1], is[2], is[3]};
@@ -130,6 +131,13 @@ extern "C" int nt_b200_conv2d(const void *input, const void *filter, void *outpu
     nt::simt::StoreConv<T> out{static_cast<T *>(output), P, Q, os[0], os[1], os[2], os[3]};
     return nt::simt::launch_gemm(A, B, out, n * P * Q, k, c * r * s, st);
   });
+}
+
+extern "C" int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k, int64_t r,
+                                                 int64_t s, int dtype) {
+  if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0) return 0;
+  if (!nt::is_half_dtype(dtype)) return 0;
+  return nt::tc::conv_workspace_bytes(n, c, h, w, k, r, s, 2);
 }
 
 extern "C" int nt_b200_attention(const void *q, const void *k, const void *v, int is_causal, void *o,

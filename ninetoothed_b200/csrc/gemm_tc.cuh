@@ -25,7 +25,7 @@ namespace tc {
 
 constexpr int kNotEligible = -1;
 
-enum class Epilogue { kMatmul, kAddmm };
+enum class Epilogue { kMatmul, kAddmm, kConv };
 
 struct GemmProblem {
   const void *a, *b, *bias;
@@ -92,6 +92,11 @@ struct Params {
   int64_t sim, sin;
   float beta, alpha;  // rounded to TI and float16 (addmm_value)
   int tiles_m, tiles_n, num_kb;
+  // conv2d implicit GEMM (EPI == kConv): output tile = BP x BQ output pixels of
+  // one image; k-block kb = (r, s, channel block cb).
+  int conv_c_blocks, conv_s, conv_pad_h, conv_pad_w;
+  int conv_bp, conv_bq, conv_p_blocks, conv_q_blocks, conv_P, conv_Q;
+  int64_t conv_osn, conv_osk, conv_osp, conv_osq;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int &mb, int &nb) {
@@ -125,6 +130,16 @@ __device__ __forceinline__ void store_row_chunk(TO *dst, const float (&v)[32], b
     for (int e = 0; e < 32; ++e)
       if (e < valid) dst[e] = from_f<TO>(v[e]);
   }
+}
+
+// Output-tile origin of a conv2d m-block: image, first output row, first column.
+__device__ __forceinline__ void conv_tile(const Params &prm, int mb, int &img, int &p0, int &q0) {
+  const int qb = mb % prm.conv_q_blocks;
+  const int t = mb / prm.conv_q_blocks;
+  const int pb = t % prm.conv_p_blocks;
+  img = t / prm.conv_p_blocks;
+  p0 = pb * prm.conv_bp;
+  q0 = qb * prm.conv_bq;
 }
 
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
@@ -188,6 +203,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
           const int k0 = kb * BK;
+          if constexpr (EPI == Epilogue::kConv) {
+            // A: BP x BQ pixels x 64 channels of the NHWC input at filter tap
+            // (r, s); coordinates outside the image read as zero (the padding).
+            // B: 256 output channels x 64 input channels of the KRSC filter.
+            const int cb = kb % prm.conv_c_blocks, rs = kb / prm.conv_c_blocks;
+            const int r = rs / prm.conv_s, sx = rs % prm.conv_s;
+            int img, p0, q0;
+            conv_tile(prm, mb, img, p0, q0);
+            ptx::tma_load_4d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, cb * BK, q0 + sx - prm.conv_pad_w,
+                             p0 + r - prm.conv_pad_h, img);
+            ptx::tma_load_3d(b_base + stage * B_STAGE_BYTES, &tmap_b, fb, cb * BK, rs, n0);
+          } else {
           ptx::tma_load_2d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, k0, m0);
           if constexpr (B_MN_MAJOR) {
 #pragma unroll
@@ -195,6 +222,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
               ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES + j * (BK * 128), &tmap_b, fb, n0 + 64 * j, k0);
           } else {
             ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES, &tmap_b, fb, k0, n0);
+          }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -251,6 +279,28 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const int64_t n0 = (int64_t)nb * BN;
       const bool row_ok = m < prm.M;
       TO *out = static_cast<TO *>(prm.out);
+      if constexpr (EPI == Epilogue::kConv) {
+        // TMEM lane = pixel (hp, wq) of the tile; columns = output channels.
+        int img, p0, q0;
+        conv_tile(prm, mb, img, p0, q0);
+        const int p = p0 + row_in_tile / prm.conv_bq, q = q0 + row_in_tile % prm.conv_bq;
+        const bool pix_ok = p < prm.conv_P && q < prm.conv_Q;
+        TO *pix = out + (int64_t)img * prm.conv_osn + (int64_t)p * prm.conv_osp + (int64_t)q * prm.conv_osq;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t raw[32];
+          ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32),
+                                  raw);
+          ptx::tmem_ld_wait();
+          const int64_t nc = n0 + c * 32;
+          if (!pix_ok || nc >= prm.N) continue;
+          const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
+          TO *dst = pix + nc * prm.conv_osk;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (e < valid) dst[e * prm.conv_osk] = from_f<TO>(round_f16(__uint_as_float(raw[e])));
+        }
+      } else {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t raw[32];
@@ -263,7 +313,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         if constexpr (EPI == Epilogue::kMatmul) {
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
-        } else {
+        } else if constexpr (EPI == Epilogue::kAddmm) {
           const TI *bias = static_cast<const TI *>(prm.bias) + m * prm.sim + nc * prm.sin;
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
@@ -278,6 +328,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         } else {
           for (int e = 0; e < valid; ++e) dst[e * prm.son] = from_f<TO>(v[e]);
         }
+      }
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(buf));
@@ -344,11 +395,148 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
   }
 }
 
+// ------------------------------------------------------------------ conv2d staging
+// NCHW (any strides) -> dense NHWC, one 64-channel x 64-pixel tile per CTA
+// through shared memory, so both the reads (along pixels) and the writes
+// (along channels) are contiguous runs.
 template <typename T>
-int try_conv(const ConvProblem &p, cudaStream_t stream) {
-  (void)p;
-  (void)stream;
-  return kNotEligible;
+__global__ void __launch_bounds__(256)
+nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int64_t isn, int64_t isc,
+                    int64_t ish, int64_t isw) {
+  __shared__ T tile[64][64 + 2];
+  const int n = blockIdx.z, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
+  const int t = threadIdx.x;
+  const T *src = in + (int64_t)n * isn;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int cc = t / 64 + 4 * i, pp = t % 64;
+    const int c = c0 + cc, pix = p0 + pp;
+    if (c < C && pix < HW) tile[cc][pp] = src[(int64_t)c * isc + (int64_t)(pix / W) * ish + (int64_t)(pix % W) * isw];
+  }
+  __syncthreads();
+  T *dst = out + (int64_t)n * HW * C;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int pp = t / 64 + 4 * i, cc = t % 64;
+    const int c = c0 + cc, pix = p0 + pp;
+    if (c < C && pix < HW) dst[(int64_t)pix * C + c] = tile[cc][pp];
+  }
+}
+
+// KCRS filter (any strides) -> dense KRSC.
+template <typename T>
+__global__ void kcrs_to_krsc_kernel(const T *__restrict__ in, T *__restrict__ out, int K, int C, int R, int S,
+                                    int64_t sk, int64_t sc, int64_t sr, int64_t ss) {
+  const int64_t total = (int64_t)K * R * S * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    int64_t t = i / C;
+    const int sx = (int)(t % S);
+    t /= S;
+    const int r = (int)(t % R);
+    const int k = (int)(t / R);
+    out[i] = in[k * sk + c * sc + r * sr + sx * ss];
+  }
+}
+
+// Workspace of the tensor-core conv2d path: dense NHWC input, then the KRSC
+// filter at the next 256-byte boundary.  0 when the path does not apply.
+inline int64_t conv_workspace_bytes(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k, int64_t r, int64_t s,
+                                    int elem) {
+  if (elem != 2 || c % 8 != 0) return 0;
+  const int64_t act = n * h * w * c * elem;
+  const int64_t flt = k * r * s * c * elem;
+  return ((act + 255) / 256) * 256 + flt;
+}
+
+template <typename T>
+int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  if constexpr (sizeof(T) != 2) {
+    return kNotEligible;
+  } else {
+    using namespace gemm;
+    const int64_t need = conv_workspace_bytes(p.n, p.c, p.h, p.w, p.k, p.r, p.s, 2);
+    if (need == 0 || workspace == nullptr || workspace_bytes < need) return kNotEligible;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kNotEligible;
+    if (p.n > (1 << 16) || p.c > (1 << 20) || p.h > (1 << 20) || p.w > (1 << 20) || p.k > (1 << 20) ||
+        p.r * p.s > (1 << 20) || p.h * p.w > (1LL << 31) - 1)
+      return kNotEligible;
+    // Output tile: BP rows x BQ columns of one image, BQ the power of two >= Q
+    // (at most 128), BP * BQ = 128 pixels.
+    int bq = 1;
+    while (bq < p.Q && bq < 128) bq <<= 1;
+    if (bq < 8) bq = 8;  // 16 rows at most per tile
+    const int bp = BM / bq;
+    T *act = static_cast<T *>(workspace);
+    T *flt = reinterpret_cast<T *>(static_cast<uint8_t *>(workspace) + ((p.n * p.h * p.w * p.c * 2 + 255) / 256) * 256);
+    {
+      const int HW = (int)(p.h * p.w);
+      dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)p.n);
+      nchw_to_nhwc_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW, (int)p.w,
+                                                       p.is[0], p.is[1], p.is[2], p.is[3]);
+      const int64_t total = p.k * p.r * p.s * p.c;
+      const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+      kcrs_to_krsc_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T *>(p.filter), flt, (int)p.k, (int)p.c,
+                                                         (int)p.r, (int)p.s, p.fs[0], p.fs[1], p.fs[2], p.fs[3]);
+      const int st = launch_status();
+      if (st != 0) return st;
+    }
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return kNotEligible;
+    CUtensorMap ta, tb;
+    {
+      const cuuint64_t dims[4] = {(cuuint64_t)p.c, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
+      const cuuint64_t strides[3] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.w * p.c * 2),
+                                     (cuuint64_t)(p.h * p.w * p.c * 2)};
+      const cuuint32_t box[4] = {64, (cuuint32_t)bq, (cuuint32_t)bp, 1};
+      const cuuint32_t estr[4] = {1, 1, 1, 1};
+      if (fn(&ta, tmap_dtype<T>(), 4, act, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return kNotEligible;
+    }
+    {
+      const cuuint64_t dims[3] = {(cuuint64_t)p.c, (cuuint64_t)(p.r * p.s), (cuuint64_t)p.k};
+      const cuuint64_t strides[2] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.r * p.s * p.c * 2)};
+      const cuuint32_t box[3] = {64, 1, (cuuint32_t)BN};
+      const cuuint32_t estr[3] = {1, 1, 1};
+      if (fn(&tb, tmap_dtype<T>(), 3, flt, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return kNotEligible;
+    }
+    Params prm{};
+    prm.out = p.output;
+    prm.conv_c_blocks = (int)((p.c + BK - 1) / BK);
+    prm.conv_s = (int)p.s;
+    prm.conv_pad_h = (int)p.pad_h;
+    prm.conv_pad_w = (int)p.pad_w;
+    prm.conv_bp = bp;
+    prm.conv_bq = bq;
+    prm.conv_p_blocks = (int)((p.P + bp - 1) / bp);
+    prm.conv_q_blocks = (int)((p.Q + bq - 1) / bq);
+    prm.conv_P = (int)p.P;
+    prm.conv_Q = (int)p.Q;
+    prm.conv_osn = p.os[0];
+    prm.conv_osk = p.os[1];
+    prm.conv_osp = p.os[2];
+    prm.conv_osq = p.os[3];
+    const int64_t tiles_m = p.n * prm.conv_p_blocks * prm.conv_q_blocks;
+    prm.tiles_m = (int)tiles_m;
+    prm.tiles_n = (int)((p.k + BN - 1) / BN);
+    prm.num_kb = (int)(p.r * p.s * prm.conv_c_blocks);
+    prm.M = tiles_m * BM;
+    prm.N = p.k;
+    prm.K = p.r * p.s * p.c;
+    const int64_t tiles = tiles_m * prm.tiles_n;
+    if (tiles > (1LL << 30)) return kNotEligible;
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    auto kern = gemm_kernel<T, T, Epilogue::kConv, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, prm);
+    return launch_status();
+  }
 }
 
 }  // namespace tc

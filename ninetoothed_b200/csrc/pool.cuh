@@ -3,10 +3,8 @@
 //
 // Window positions outside the input are skipped, which is the same as the
 // reference's `other=-inf` fill for a max.  The result is an element of the
-// input, so it is bit-exact.  One thread per output element, with consecutive
-// threads on consecutive output columns: the window rows a warp reads are
-// contiguous runs of the input row, and the overlap between neighbouring
-// windows is served from L1.
+// input, so it is bit-exact.  Neighbouring windows overlap; the overlap is
+// served from L1, so HBM sees each input element about once.
 #pragma once
 
 #include "common.cuh"
@@ -47,74 +45,63 @@ max_pool2d_kernel(const T *__restrict__ in, T *__restrict__ out, int64_t n, int6
   }
 }
 
-// Plane-tiled path for planes with unit column stride: a CTA stages the input
-// rows that a band of output rows needs in shared memory (16-byte vector loads
-// when the band is aligned, so every input byte is read from HBM once) and
-// computes the band's outputs from there with 32-bit index math.
-constexpr int kPlaneThreads = 256;
-constexpr int kPlaneSmemBytes = 32 * 1024;
-
-template <typename T>
-__global__ void __launch_bounds__(kPlaneThreads)
-max_pool2d_plane_kernel(const T *__restrict__ in, T *__restrict__ out, int c, int h, int w, int64_t isn,
-                        int64_t isc, int64_t ish, int out_h, int out_w, int64_t osn, int64_t osc, int64_t osh,
-                        int64_t osw, int wh, int ww, int sh, int sw, int ph, int pw, int band, int bands) {
-  __shared__ __align__(16) unsigned char smem_raw[kPlaneSmemBytes];
-  T *tile = reinterpret_cast<T *>(smem_raw);
-  const int64_t plane = blockIdx.x / bands;
-  const int band_idx = blockIdx.x % bands;
-  const int ni = (int)(plane / c), ci = (int)(plane % c);
-  const int p0 = band_idx * band;
-  const int p1 = min(p0 + band, out_h);
-  const int y0 = max(p0 * sh - ph, 0);
-  const int y1 = min((p1 - 1) * sh - ph + wh, h);  // exclusive
-  const int rows = y1 - y0;
-  const T *src = in + ni * isn + ci * isc + (int64_t)y0 * ish;
-  const int count = rows * w;
-  constexpr int E = 16 / sizeof(T);
-  const bool packed = ish == w && (reinterpret_cast<uintptr_t>(src) % 16) == 0 && (count % E) == 0;
-  if (packed) {
-    const int4 *v = reinterpret_cast<const int4 *>(src);
-    int4 *t = reinterpret_cast<int4 *>(tile);
-    for (int i = threadIdx.x; i < count / E; i += kPlaneThreads) t[i] = __ldcs(v + i);
-  } else {
-    for (int i = threadIdx.x; i < count; i += kPlaneThreads) {
-      const int r = i / w, x = i - r * w;
-      tile[i] = src[(int64_t)r * ish + x];
-    }
-  }
-  __syncthreads();
-  T *dst = out + ni * osn + ci * osc;
-  const int outputs = (p1 - p0) * out_w;
-  for (int i = threadIdx.x; i < outputs; i += kPlaneThreads) {
-    const int pp = p0 + i / out_w, q = i % out_w;
-    const int ys = pp * sh - ph, xs = q * sw - pw;
-    float m = -INFINITY;
-    for (int r = 0; r < wh; ++r) {
-      const int y = ys + r;
-      if (y < 0 || y >= h) continue;
-      const T *row = tile + (y - y0) * w;
-      for (int s2 = 0; s2 < ww; ++s2) {
-        const int x = xs + s2;
-        if (x < 0 || x >= w) continue;
-        const float v = to_f(row[x]);
-        m = v > m ? v : m;
+// Row path for inputs and outputs with unit column stride: one warp per output
+// row (n, c, p), lanes over the output columns, so index arithmetic is per row
+// and a warp's loads are one contiguous run of the input row.  WH/WW/SH/SW > 0
+// fix the window and stride at compile time (fully unrolled, all window loads
+// in flight together); 0 takes them from the arguments.
+template <typename T, int WH, int WW, int SH, int SW>
+__global__ void __launch_bounds__(256)
+max_pool2d_rows_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
+                       int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp, int64_t rows,
+                       int wh_, int ww_, int sh_, int sw_, int ph, int pw) {
+  const int wh = WH > 0 ? WH : wh_, ww = WW > 0 ? WW : ww_;
+  const int sh = SH > 0 ? SH : sh_, sw = SW > 0 ? SW : sw_;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * 8) {
+    const int p = (int)(row % P);
+    const int64_t nc = row / P;
+    const int ci = (int)(nc % C);
+    const int64_t ni = nc / C;
+    const T *plane = in + ni * isn + ci * isc;
+    T *orow = out + ni * osn + ci * osc + p * osp;
+    const int y0 = p * sh - ph;
+    for (int q = lane; q < Q; q += 32) {
+      const int x0 = q * sw - pw;
+      float m = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < (WH > 0 ? WH : 1); ++r) {
+        for (int rr = (WH > 0 ? r : 0); rr < (WH > 0 ? r + 1 : wh); ++rr) {
+          const int y = y0 + rr;
+          if (y < 0 || y >= H) continue;
+          const T *irow = plane + y * ish;
+#pragma unroll
+          for (int s2 = 0; s2 < (WW > 0 ? WW : 1); ++s2) {
+            for (int ss = (WW > 0 ? s2 : 0); ss < (WW > 0 ? s2 + 1 : ww); ++ss) {
+              const int x = x0 + ss;
+              if (x < 0 || x >= W) continue;
+              const float v = to_f(irow[x]);
+              m = v > m ? v : m;
+            }
+          }
+        }
       }
+      orow[q] = from_f<T>(m);
     }
-    dst[pp * osh + q * osw] = from_f<T>(m);
   }
 }
 
-// Output rows per CTA so that the staged input band fits kPlaneSmemBytes;
-// 0 when even one output row does not fit.
-inline int plane_band(int64_t out_h, int64_t w, int64_t wh, int64_t sh, int elem) {
-  const int64_t row_bytes = w * elem;
-  if (row_bytes <= 0) return 0;
-  const int64_t max_rows = kPlaneSmemBytes / row_bytes;
-  if (max_rows < wh) return 0;
-  int64_t band = (max_rows - wh) / sh + 1;
-  if (band > out_h) band = out_h;
-  return (int)band;
+template <typename T, int WH, int WW, int SH, int SW>
+inline void launch_rows(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
+                        int64_t P, int64_t Q, const int64_t *os, int64_t wh, int64_t ww, int64_t sh, int64_t sw,
+                        int64_t ph, int64_t pw, cudaStream_t stream) {
+  const int64_t rows = n * c * P;
+  int64_t grid = (rows + 7) / 8;
+  const int64_t cap = (int64_t)sm_count() * 32;
+  if (grid > cap) grid = cap;
+  max_pool2d_rows_kernel<T, WH, WW, SH, SW><<<(unsigned)grid, 256, 0, stream>>>(
+      in, out, (int)c, (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], rows, (int)wh,
+      (int)ww, (int)sh, (int)sw, (int)ph, (int)pw);
 }
 
 }  // namespace pool
@@ -138,19 +125,23 @@ extern "C" int nt_b200_max_pool2d(const void *input, void *output, int64_t n, in
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t *is = input_strides, *os = output_strides;
   return NT_DISPATCH_FLOAT(dtype, [&] {
-    const int band = nt::pool::plane_band(out_h, w, window_h, stride_h, (int)sizeof(scalar_t));
+    // The row path keeps the in-plane offsets (y * row stride + x) in 32 bits.
     const bool int32_ok = h < (1 << 30) && w < (1 << 30) && out_h < (1 << 30) && out_w < (1 << 30) &&
-                          h * w < (1LL << 31) && out_h * out_w < (1LL << 31);
-    if (is[3] == 1 && band > 0 && int32_ok) {
-      const int64_t bands = (out_h + band - 1) / band;
-      const int64_t grid = n * c * bands;
-      if (grid < (1LL << 31)) {
-        nt::pool::max_pool2d_plane_kernel<scalar_t><<<(unsigned)grid, nt::pool::kPlaneThreads, 0, s>>>(
-            static_cast<const scalar_t *>(input), static_cast<scalar_t *>(output), (int)c, (int)h, (int)w, is[0],
-            is[1], is[2], (int)out_h, (int)out_w, os[0], os[1], os[2], os[3], (int)window_h, (int)window_w,
-            (int)stride_h, (int)stride_w, (int)pad_h, (int)pad_w, band, (int)bands);
-        return nt::launch_status();
-      }
+                          c < (1 << 30) && (h + 1) * (is[2] < 0 ? -is[2] : is[2]) < (1LL << 31);
+    if (is[3] == 1 && os[3] == 1 && int32_ok) {
+      using T = scalar_t;
+      const T *in = static_cast<const T *>(input);
+      T *out = static_cast<T *>(output);
+      if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2)
+        nt::pool::launch_rows<T, 3, 3, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, 3, 3, 2, 2, pad_h, pad_w, s);
+      else if (window_h == 3 && window_w == 3 && stride_h == 3 && stride_w == 3)
+        nt::pool::launch_rows<T, 3, 3, 3, 3>(in, out, n, c, h, w, is, out_h, out_w, os, 3, 3, 3, 3, pad_h, pad_w, s);
+      else if (window_h == 2 && window_w == 2 && stride_h == 2 && stride_w == 2)
+        nt::pool::launch_rows<T, 2, 2, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, 2, 2, 2, 2, pad_h, pad_w, s);
+      else
+        nt::pool::launch_rows<T, 0, 0, 0, 0>(in, out, n, c, h, w, is, out_h, out_w, os, window_h, window_w,
+                                              stride_h, stride_w, pad_h, pad_w, s);
+      return nt::launch_status();
     }
     const int64_t total = n * c * out_h * out_w;
     const int threads = 256;

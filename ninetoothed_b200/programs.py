@@ -144,9 +144,14 @@ def _launch_conv2d(v, stream):
     if c2 != c or tuple(out.shape) != (n, k, p, q):
         raise TypeError(f"conv2d output has shape {tuple(out.shape)}; expected {(n, k, p, q)}.")
     xs, ws, os_ = (_lib.int64_array(t.stride()) for t in (x, w, out))
+    code = dtype_code(x.dtype)
+    # Workspace for the NHWC / KRSC staging of the tensor-core path, from the
+    # caching allocator on the launch stream (the C ABI never allocates).
+    nbytes = _lib_call("nt_b200_conv2d_workspace_size", n, c, h, wd, k, r, s, code)
+    workspace = torch.empty(max(nbytes, 0), dtype=torch.uint8, device=x.device) if nbytes > 0 else None
     return _lib_call(
-        "nt_b200_conv2d", ptr(x), ptr(w), ptr(out), n, c, h, wd, k, r, s, ph, pw, xs, ws, os_, dtype_code(x.dtype),
-        stream,
+        "nt_b200_conv2d", ptr(x), ptr(w), ptr(out), n, c, h, wd, k, r, s, ph, pw, xs, ws, os_,
+        ptr(workspace) if workspace is not None else None, nbytes, code, stream,
     )
 
 

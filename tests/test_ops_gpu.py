@@ -37,6 +37,15 @@ def _steps(ref, dtype):
     return np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
 
 
+def addmm_abs_sum(a, b, alpha):
+    """Error scale of addmm: a one-step difference in the float16-rounded
+    accumulator is scaled by alpha before the final rounding, so the bound adds
+    two float16 steps at |alpha * acc| to the summation-order term."""
+    acc = oracle.matmul(a, b, "float32")
+    bound = abs(alpha) * oracle.matmul(np.abs(oracle._f32(a)), np.abs(oracle._f32(b)), "float32")
+    return bound + 2 * _steps(np.abs(alpha * acc), torch.float16) * 2.0 ** 20
+
+
 def assert_within_steps(got, ref, dtype, steps=2, abs_sum=None):
     """|got - ref| <= steps rounding steps of `dtype` at |ref|, plus the fp32
     summation-order bound 2^-20 * sum_k |a_k b_k| when `abs_sum` is given (two
@@ -233,15 +242,14 @@ def test_addmm_reference_case():
     out = programs.addmm(inp, a, b, beta=beta, alpha=alpha)
     assert torch.allclose(out, torch.addmm(inp, a, b, beta=beta, alpha=alpha), atol=0.075)
     ref = oracle.addmm(inp.cpu(), a.cpu(), b.cpu(), beta, alpha, "float16")
-    bound = alpha * oracle.matmul(a.cpu().abs(), b.cpu().abs(), "float32")
-    assert_within_steps(_np(out), ref, torch.float16, abs_sum=bound)
+    assert_within_steps(_np(out), ref, torch.float16, abs_sum=addmm_abs_sum(a.cpu(), b.cpu(), alpha))
 
 
 def test_addmm_golden():
     g = golden_io.load("addmm_f16_48x64x80")
     t = {k: golden_io.tensor(g[k], DEV) for k in ("input", "mat1", "mat2")}
     out = programs.addmm(t["input"], t["mat1"], t["mat2"], beta=float(g["beta"]), alpha=float(g["alpha"]))
-    bound = oracle.matmul(np.abs(g["mat1"].astype(np.float32)), np.abs(g["mat2"].astype(np.float32)), "float32")
+    bound = addmm_abs_sum(g["mat1"], g["mat2"], float(g["alpha"]))
     assert_within_steps(_np(out), g["output"].astype(np.float32), torch.float16, abs_sum=bound)
 
 
@@ -253,8 +261,7 @@ def test_addmm_baseline_config_sampled_rows():
     out = programs.addmm(inp.to(DEV), a.to(DEV), b.to(DEV), beta=1.0, alpha=1.0, out_dtype=torch.bfloat16)
     rows = torch.tensor([0, 1, 127, 128, 4095, 8191])
     ref = oracle.addmm(inp[rows], a[rows], b, 1.0, 1.0, "bfloat16")
-    bound = oracle.matmul(a[rows].abs(), b.abs(), "float32")
-    assert_within_steps(_np(out[rows.to(DEV)]), ref, torch.bfloat16, abs_sum=bound)
+    assert_within_steps(_np(out[rows.to(DEV)]), ref, torch.bfloat16, abs_sum=addmm_abs_sum(a[rows], b, 1.0))
 
 
 # ----------------------------------------------------------------- attention
