@@ -174,7 +174,8 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ timing helpers
 def time_launches(fn, steps, stream):
-    """Device time (ms) of `steps` calls of fn(i) on `stream`, CUDA events."""
+    """Device time (ms) of `steps` eager calls of fn(i) on `stream`, CUDA
+    events (includes any host-side gap between launches)."""
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     start.record(stream)
@@ -185,17 +186,32 @@ def time_launches(fn, steps, stream):
     return start.elapsed_time(end)
 
 
-def soak(fn, seconds):
-    """Runs fn back to back for about `seconds` (untimed) so that clock samples
-    cover a loaded GPU around the timed region."""
-    t0 = time.perf_counter()
-    i = 0
-    while time.perf_counter() - t0 < seconds:
-        fn(i)
-        i += 1
-        if i % 64 == 0:
-            torch.cuda.synchronize()
+def capture_steps(fn, steps):
+    """A CUDA graph of `steps` calls fn(0..steps-1): the launches replay back to
+    back with no host work between them."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn(0)
+    torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(steps):
+            fn(i)
+    torch.cuda.synchronize()
+    return graph
+
+
+def time_graph(graph, stream):
+    """Device time (ms) of one replay of `graph`, CUDA events on `stream`."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
 
 
 # ------------------------------------------------------------------ reference arm
@@ -278,8 +294,11 @@ def bench_ops(which, steps, dist, peaks):
     def record(name, fn, work, unit, peak, nsteps=steps, warm=3):
         for i in range(warm):
             fn(i)
+        graph = capture_steps(fn, nsteps)
+        graph.replay()
         dist.barrier()
-        ms = dist.max(time_launches(fn, nsteps, stream)) / nsteps
+        ms = dist.max(time_graph(graph, stream)) / nsteps
+        del graph
         if unit == "TFLOP/s":
             achieved = work / (ms * 1e-3) / 1e12
         else:
@@ -382,8 +401,12 @@ def run_single(args):
     for _ in range(args.warmup):
         fn()
     ms = time_launches(lambda i: fn(), args.steps, torch.cuda.current_stream()) / max(args.steps, 1)
-    rate = work / (ms * 1e-3) / (1e12 if unit == "TFLOP/s" else 1e9)
-    print(json.dumps({"only": op, "ms": ms, "value": rate, "unit": unit, "launches": args.warmup + args.steps}))
+    graph = capture_steps(lambda i: fn(), max(args.steps, 1))
+    graph_ms = time_graph(graph, torch.cuda.current_stream()) / max(args.steps, 1)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    print(json.dumps({"only": op, "ms_eager": ms, "value_eager": work / (ms * 1e-3) / scale, "ms_graph": graph_ms,
+                      "value_graph": work / (graph_ms * 1e-3) / scale, "unit": unit,
+                      "launches": args.warmup + 3 * args.steps}))
 
 
 # ------------------------------------------------------------------ main arm
@@ -409,14 +432,22 @@ def run_b200(args, dist):
         step(i)
     torch.cuda.synchronize()
 
+    # The timed K steps are one CUDA graph of K launches (no host work between
+    # them), replayed once between events; the soak before it replays the same
+    # graph so the clock samples see a loaded GPU.
+    graph = capture_steps(step, args.steps)
     sampler = ClockSampler(dev.index)
     sampler.start()
-    soak(step, args.soak_seconds)
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < args.soak_seconds:
+        graph.replay()
+        torch.cuda.synchronize()
     dist.barrier()
     torch.cuda.synchronize()
-    elapsed_ms = dist.max(time_launches(step, args.steps, stream))
+    elapsed_ms = dist.max(time_graph(graph, stream))
     dist.barrier()
     clocks = sampler.stop()
+    del graph
     ms = elapsed_ms / args.steps
     value = SOFTMAX_BYTES * dist.world / (ms * 1e-3) / 1e9
     achieved = SOFTMAX_BYTES / (ms * 1e-3) / 1e9  # one launch per step

@@ -42,33 +42,55 @@ struct AttentionProblem {
 
 namespace attn {
 
-constexpr int BM = 128;  // queries per CTA
-constexpr int BN = 128;  // keys per block
-constexpr int THREADS = 192;
+constexpr int BM = 128;     // queries per Q tile
+constexpr int BN = 128;     // keys per block
+constexpr int TILES = 2;    // Q tiles per CTA, one softmax warpgroup each
+constexpr int RING = 3;     // K/V shared-memory slots (K_j, V_j, K_j+1, ... in load order)
+constexpr int THREADS = 64 + TILES * 128;
 constexpr int TMEM_COLS = 512;
+// A row's running max is only moved when a block's max exceeds it by more
+// than 2^8 (log2 domain); otherwise p = exp2(s - m) <= 256 against the stale
+// max.  o / l is unchanged mathematically, and O is rescaled in TMEM far less
+// often.
+constexpr float kRescaleThreshold = 8.0f;
 
 template <int DP>  // head_dim padded to 64 or 128
 struct Layout {
   static constexpr int ATOMS = DP / 64;                // 128-byte swizzle atoms along head_dim
-  static constexpr int Q_BYTES = BM * DP * 2;
+  static constexpr int Q_BYTES = BM * DP * 2;          // one Q tile
   static constexpr int KV_BYTES = BN * DP * 2;         // one K or V block
-  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int P_BYTES = BM * BN * 2;          // one P tile
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = Q_OFF + Q_BYTES;        // 2 stages
-  static constexpr int V_OFF = K_OFF + 2 * KV_BYTES;   // 2 stages
-  static constexpr int P_OFF = V_OFF + 2 * KV_BYTES;
-  static constexpr int CTRL_OFF = P_OFF + P_BYTES;
+  static constexpr int RING_OFF = Q_OFF + TILES * Q_BYTES;
+  static constexpr int P_OFF = RING_OFF + RING * KV_BYTES;
+  static constexpr int CTRL_OFF = P_OFF + TILES * P_BYTES;
   static constexpr int SMEM_BYTES = CTRL_OFF + 256 + 1024;
 };
 
 struct Params {
   int B, H, SQ, SK, D;
-  int q_tiles;
+  int q_pairs;  // CTAs per (batch, head): ceil(SQ / (TILES * BM))
   int causal;
   float log2e;
   void *o;
   int64_t osb, osh, oss, osd;
 };
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
 
 template <typename T, int DP>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -82,39 +104,42 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
   const uint32_t ctrl = base + L::CTRL_OFF;
   // barrier slots (8 bytes each)
   const uint32_t q_full = ctrl + 0, q_ready = ctrl + 8;
-  auto k_full = [&](int s) { return ctrl + 16 + 8u * s; };
-  auto v_full = [&](int s) { return ctrl + 32 + 8u * s; };
-  auto kv_empty = [&](int s) { return ctrl + 48 + 8u * s; };
-  auto s_full = [&](int b) { return ctrl + 64 + 8u * b; };
-  auto s_free = [&](int b) { return ctrl + 80 + 8u * b; };
-  const uint32_t p_full = ctrl + 96, o_done = ctrl + 104;
+  auto slot_full = [&](int s) { return ctrl + 16 + 8u * s; };
+  auto slot_empty = [&](int s) { return ctrl + 40 + 8u * s; };
+  auto s_full = [&](int t) { return ctrl + 64 + 8u * t; };
+  auto p_full = [&](int t) { return ctrl + 80 + 8u * t; };
+  auto o_done = [&](int t) { return ctrl + 96 + 8u * t; };
   volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(smem + L::CTRL_OFF + 128);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::CTRL_OFF + 132);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // Work item: heavy (late) query tiles first for causal balance.
-  const int per_head = prm.q_tiles;
+  // Work item (batch, head, pair of Q tiles); causal pairs run longest first.
+  const int per_head = prm.q_pairs;
   const int bh = blockIdx.x / per_head;
-  const int qt = prm.causal ? per_head - 1 - (int)(blockIdx.x % per_head) : (int)(blockIdx.x % per_head);
+  const int qp = prm.causal ? per_head - 1 - (int)(blockIdx.x % per_head) : (int)(blockIdx.x % per_head);
   const int b = bh / prm.H, h = bh % prm.H;
-  const int q0 = qt * BM;
-  const int kv_blocks_total = (prm.SK + BN - 1) / BN;
-  int n_blocks = kv_blocks_total;
-  if (prm.causal) n_blocks = min(n_blocks, (q0 + BM - 1) / BN + 1);
+  const int q0 = qp * (TILES * BM);
+  const int kv_blocks = (prm.SK + BN - 1) / BN;
+  // key blocks each Q tile needs (causal: up to its diagonal block)
+  int n_blk[TILES];
+#pragma unroll
+  for (int t = 0; t < TILES; ++t)
+    n_blk[t] = prm.causal ? min(kv_blocks, (q0 + t * BM + BM - 1) / BN + 1) : kv_blocks;
+  const int n_max = n_blk[TILES - 1];
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(q_full, 1);
-    ptx::mbar_init(q_ready, 128);
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(k_full(s), 1);
-      ptx::mbar_init(v_full(s), 1);
-      ptx::mbar_init(kv_empty(s), 1);
-      ptx::mbar_init(s_full(s), 1);
-      ptx::mbar_init(s_free(s), 128);
+    ptx::mbar_init(q_ready, TILES * 128);
+    for (int s = 0; s < RING; ++s) {
+      ptx::mbar_init(slot_full(s), 1);
+      ptx::mbar_init(slot_empty(s), 1);
     }
-    ptx::mbar_init(p_full, 128);
-    ptx::mbar_init(o_done, 1);
+    for (int t = 0; t < TILES; ++t) {
+      ptx::mbar_init(s_full(t), 1);
+      ptx::mbar_init(p_full(t), 128);
+      ptx::mbar_init(o_done(t), 1);
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmap_q);
@@ -129,94 +154,107 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_base_ptr;
-  const uint32_t tmem_s0 = tmem_base, tmem_o = tmem_base + 2 * BN;
+  auto tmem_s = [&](int t) { return tmem_base + (uint32_t)(t * BN); };
+  auto tmem_o = [&](int t) { return tmem_base + (uint32_t)(TILES * BN + t * 128); };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      ptx::mbar_arrive_expect_tx(q_full, L::Q_BYTES);
-      for (int a = 0; a < L::ATOMS; ++a)
-        ptx::tma_load_4d(base + L::Q_OFF + a * (BM * 128), &tmap_q, q_full, 64 * a, q0, h, b);
-      for (int j = 0; j < n_blocks; ++j) {
-        const int s = j & 1;
-        const uint32_t use = (uint32_t)(j >> 1) & 1u;
-        if (!ptx::mbar_wait(kv_empty(s), use ^ 1u, abort_flag)) break;
-        ptx::mbar_arrive_expect_tx(k_full(s), L::KV_BYTES);
+      ptx::mbar_arrive_expect_tx(q_full, TILES * L::Q_BYTES);
+      for (int t = 0; t < TILES; ++t)
         for (int a = 0; a < L::ATOMS; ++a)
-          ptx::tma_load_4d(base + L::K_OFF + s * L::KV_BYTES + a * (BN * 128), &tmap_k, k_full(s), 64 * a, j * BN,
+          ptx::tma_load_4d(base + L::Q_OFF + t * L::Q_BYTES + a * (BM * 128), &tmap_q, q_full, 64 * a, q0 + t * BM,
                            h, b);
-        ptx::mbar_arrive_expect_tx(v_full(s), L::KV_BYTES);
+      // ring items in order K_0, V_0, K_1, V_1, ...
+      for (int i = 0; i < 2 * n_max; ++i) {
+        const int slot = i % RING;
+        const uint32_t use = (uint32_t)(i / RING) & 1u;
+        if (!ptx::mbar_wait(slot_empty(slot), use ^ 1u, abort_flag)) break;
+        ptx::mbar_arrive_expect_tx(slot_full(slot), L::KV_BYTES);
+        const CUtensorMap *map = (i & 1) ? &tmap_v : &tmap_k;
         for (int a = 0; a < L::ATOMS; ++a)
-          ptx::tma_load_4d(base + L::V_OFF + s * L::KV_BYTES + a * (BN * 128), &tmap_v, v_full(s), 64 * a, j * BN,
-                           h, b);
+          ptx::tma_load_4d(base + L::RING_OFF + slot * L::KV_BYTES + a * (BN * 128), map, slot_full(slot), 64 * a,
+                           (i >> 1) * BN, h, b);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t fmt = umma_format<T>();
-      constexpr uint32_t idesc_qk = ptx::f16_idesc(fmt, 0, 0, BM, BN);   // B = K block, K-major
-      constexpr uint32_t idesc_pv = ptx::f16_idesc(fmt, 0, 1, BM, DP);   // B = V block, MN-major
-      bool ok = ptx::mbar_wait(q_ready, 0, abort_flag);
-      auto issue_qk = [&](int j) {
-        const int s = j & 1;
-        const uint32_t kb = base + L::K_OFF + s * L::KV_BYTES;
+      constexpr uint32_t idesc_qk = ptx::f16_idesc(fmt, 0, 0, BM, BN);  // B = K block, K-major
+      constexpr uint32_t idesc_pv = ptx::f16_idesc(fmt, 0, 1, BM, DP);  // B = V block, MN-major
+      auto slot_addr = [&](int item) { return base + L::RING_OFF + (item % RING) * L::KV_BYTES; };
+      auto wait_item = [&](int item) {
+        return ptx::mbar_wait(slot_full(item % RING), (uint32_t)(item / RING) & 1u, abort_flag);
+      };
+      auto issue_qk = [&](int t, int j) {
+        const uint32_t kb = slot_addr(2 * j);
 #pragma unroll
         for (int kk = 0; kk < DP / 16; ++kk) {
           const uint32_t off = (kk / 4) * (BM * 128) + (kk % 4) * 32;
           const uint32_t koff = (kk / 4) * (BN * 128) + (kk % 4) * 32;
-          const uint64_t a_desc = ptx::sw128_desc(base + L::Q_OFF + off, 16, 1024);
+          const uint64_t a_desc = ptx::sw128_desc(base + L::Q_OFF + t * L::Q_BYTES + off, 16, 1024);
           const uint64_t b_desc = ptx::sw128_desc(kb + koff, 16, 1024);
-          ptx::mma_f16_ss(tmem_s0 + (uint32_t)(s * BN), a_desc, b_desc, idesc_qk, kk > 0 ? 1u : 0u);
+          ptx::mma_f16_ss(tmem_s(t), a_desc, b_desc, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        ptx::mma_commit(s_full(s));
+        ptx::mma_commit(s_full(t));
       };
-      if (ok && n_blocks > 0) {
-        ok = ptx::mbar_wait(k_full(0), 0, abort_flag);
-        if (ok) {
-          ptx::tc_fence_after();
-          issue_qk(0);
-        }
-      }
-      for (int j = 0; j < n_blocks && ok; ++j) {
-        const int s = j & 1;
-        if (j + 1 < n_blocks) {
-          const int s1 = (j + 1) & 1;
-          const uint32_t use1 = (uint32_t)((j + 1) >> 1) & 1u;
-          if (!ptx::mbar_wait(k_full(s1), use1, abort_flag)) break;
-          // S buffer s1 was last read by the softmax of block j - 1.
-          if (!ptx::mbar_wait(s_free(s1), use1 ^ 1u, abort_flag)) break;
-          ptx::tc_fence_after();
-          issue_qk(j + 1);
-        }
-        if (!ptx::mbar_wait(p_full, (uint32_t)j & 1u, abort_flag)) break;
-        if (!ptx::mbar_wait(v_full(s), (uint32_t)(j >> 1) & 1u, abort_flag)) break;
-        ptx::tc_fence_after();
-        const uint32_t vb = base + L::V_OFF + s * L::KV_BYTES;
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t vb = slot_addr(2 * j + 1);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint32_t poff = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint64_t a_desc = ptx::sw128_desc(base + L::P_OFF + poff, 16, 1024);
+          const uint64_t a_desc = ptx::sw128_desc(base + L::P_OFF + t * L::P_BYTES + poff, 16, 1024);
           const uint64_t b_desc = ptx::sw128_desc(vb + kk * 16 * 128, BN * 128, 1024);
-          ptx::mma_f16_ss(tmem_o, a_desc, b_desc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_f16_ss(tmem_o(t), a_desc, b_desc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit(o_done);
-        ptx::mma_commit(kv_empty(s));
+        ptx::mma_commit(o_done(t));
+      };
+      bool ok = ptx::mbar_wait(q_ready, 0, abort_flag) && wait_item(0);
+      if (ok) {
+        ptx::tc_fence_after();
+        for (int t = 0; t < TILES; ++t) issue_qk(t, 0);
+        ptx::mma_commit(slot_empty(0));  // K_0 read by every tile's first QK
+      }
+      for (int j = 0; j < n_max && ok; ++j) {
+        if (!wait_item(2 * j + 1)) break;  // V_j
+        bool k_next_waited = false;
+        for (int t = 0; t < TILES && ok; ++t) {
+          if (j >= n_blk[t]) continue;
+          // P_t(j) ready also means the softmax has read S_t(j), so S_t may be
+          // overwritten by the next QK of this tile.
+          if (!ptx::mbar_wait(p_full(t), (uint32_t)j & 1u, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < n_blk[t]) {
+            if (!k_next_waited) {
+              if (!wait_item(2 * j + 2)) { ok = false; break; }
+              k_next_waited = true;
+              ptx::tc_fence_after();
+            }
+            issue_qk(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        ptx::mma_commit(slot_empty((2 * j + 1) % RING));                  // V_j
+        if (k_next_waited) ptx::mma_commit(slot_empty((2 * j + 2) % RING));  // K_j+1
       }
     }
   } else {
     // ------------------------------------------------------------ softmax / correction / epilogue
+    const int t = (warp - 2) / 4;  // Q tile of this warpgroup
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // query row within the tile = TMEM lane
-    const int qi = q0 + row;
+    const int qi = q0 + t * BM + row;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int n_t = n_blk[t];
     bool ok = ptx::mbar_wait_warp(q_full, 0, abort_flag);
     if (ok) {
       // q' = round(q * round(log2 e)) in place; a thread owns its row's 128-byte
       // segment in every atom, so the swizzle does not matter.
 #pragma unroll
       for (int a = 0; a < L::ATOMS; ++a) {
-        int4 *seg = reinterpret_cast<int4 *>(smem + L::Q_OFF + a * (BM * 128) + row * 128);
+        int4 *seg = reinterpret_cast<int4 *>(smem + L::Q_OFF + t * L::Q_BYTES + a * (BM * 128) + row * 128);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           int4 raw = seg[c];
@@ -231,48 +269,61 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     ptx::mbar_arrive(q_ready);
 
     float m_i = -INFINITY, l_i = 1.f;
-    for (int j = 0; j < n_blocks && ok; ++j) {
-      const int s = j & 1;
-      if (!ptx::mbar_wait_warp(s_full(s), (uint32_t)(j >> 1) & 1u, abort_flag)) { ok = false; break; }
+    uint8_t *p_tile = smem + L::P_OFF + t * L::P_BYTES;
+    for (int j = 0; j < n_t && ok; ++j) {
+      if (!ptx::mbar_wait_warp(s_full(t), (uint32_t)j & 1u, abort_flag)) { ok = false; break; }
       ptx::tc_fence_after();
       uint32_t sr[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c)
-        ptx::tmem_ld_32x32b_x32(tmem_s0 + lane_base + (uint32_t)(s * BN + c * 32),
+        ptx::tmem_ld_32x32b_x32(tmem_s(t) + lane_base + (uint32_t)(c * 32),
                                 *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
       ptx::tmem_ld_wait();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(s_free(s));
-
-      // masks: keys past seq_kv; causal keys above the query
-      const int k0 = j * BN;
-      int limit = prm.SK - k0;  // valid keys are [0, limit)
-      if (prm.causal) limit = min(limit, qi - k0 + 1);
-      float m_blk = -INFINITY;
       float *sv = reinterpret_cast<float *>(sr);
+      if (j == n_t - 1) {
+        // the last block of a tile holds the key tail and (causal) the diagonal
+        const int k0 = j * BN;
+        int limit = prm.SK - k0;
+        if (prm.causal) limit = min(limit, qi - k0 + 1);
+#pragma unroll
+        for (int c = 0; c < BN; ++c) sv[c] = c < limit ? sv[c] : -INFINITY;
+      }
+      // 8 independent partial maxima/sums keep the reductions off one long
+      // dependency chain.
+      float mp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mp[u] = sv[u];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mp[c & 7] = fmaxf(mp[c & 7], sv[c]);
+#pragma unroll
+      for (int u = 4; u > 0; u >>= 1)
+#pragma unroll
+        for (int v = 0; v < u; ++v) mp[v] = fmaxf(mp[v], mp[v + u]);
+      const float m_blk = mp[0];
+      const bool move = m_blk > m_i + kRescaleThreshold;  // true on the first block (m_i = -inf)
+      const float m_new = move ? m_blk : m_i;
+      const float alpha = move ? ex2(m_i - m_new) : 1.f;
+      float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
-        sv[c] = c < limit ? sv[c] : -INFINITY;
-        m_blk = fmaxf(m_blk, sv[c]);
+        sv[c] = ex2(sv[c] - m_new);
+        lp[c & 7] += sv[c];
       }
-      const float m_new = fmaxf(m_i, m_blk);
-      const float alpha = exp2f(m_i - m_new);
-      float l_blk = 0.f;
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        sv[c] = exp2f(sv[c] - m_new);
-        l_blk += sv[c];
-      }
-      // O must hold P_{j-1} V_{j-1} before it is rescaled, and P's buffer must
-      // be free before it is rewritten.
+      for (int u = 4; u > 0; u >>= 1)
+#pragma unroll
+        for (int v = 0; v < u; ++v) lp[v] += lp[v + u];
+      const float l_blk = lp[0];
+      // O_t must hold P(j-1) V(j-1) before it is rescaled, and P_t's buffer
+      // must be free before it is rewritten.
       if (j > 0) {
-        if (!ptx::mbar_wait_warp(o_done, (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
+        if (!ptx::mbar_wait_warp(o_done(t), (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
           for (int c = 0; c < DP / 32; ++c) {
             uint32_t orow[32];
-            const uint32_t taddr = tmem_o + lane_base + (uint32_t)(c * 32);
+            const uint32_t taddr = tmem_o(t) + lane_base + (uint32_t)(c * 32);
             ptx::tmem_ld_32x32b_x32(taddr, orow);
             ptx::tmem_ld_wait();
 #pragma unroll
@@ -288,22 +339,22 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
       // [64a, 64a + 64); 16-byte chunk c of row r sits at chunk c ^ (r % 8).
 #pragma unroll
       for (int a = 0; a < BN / 64; ++a) {
-        uint8_t *rowp = smem + L::P_OFF + a * (BM * 128) + row * 128;
+        uint8_t *rowp = p_tile + a * (BM * 128) + row * 128;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          alignas(16) T pk[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pk[i] = from_f<T>(sv[a * 64 + c * 8 + i]);
-          *reinterpret_cast<int4 *>(rowp + ((c ^ (row & 7)) * 16)) = *reinterpret_cast<int4 *>(pk);
+          const float *e = sv + a * 64 + c * 8;
+          const int4 pk = make_int4((int)pack2<T>(e[0], e[1]), (int)pack2<T>(e[2], e[3]), (int)pack2<T>(e[4], e[5]),
+                                    (int)pack2<T>(e[6], e[7]));
+          *reinterpret_cast<int4 *>(rowp + ((c ^ (row & 7)) * 16)) = pk;
         }
       }
       ptx::fence_proxy_async_smem();
       ptx::tc_fence_before();
-      ptx::mbar_arrive(p_full);
+      ptx::mbar_arrive(p_full(t));
     }
 
     // epilogue: O / l -> global
-    if (ok && n_blocks > 0 && ptx::mbar_wait_warp(o_done, (uint32_t)(n_blocks - 1) & 1u, abort_flag)) {
+    if (ok && n_t > 0 && ptx::mbar_wait_warp(o_done(t), (uint32_t)(n_t - 1) & 1u, abort_flag)) {
       ptx::tc_fence_after();
       const float inv = 1.f / l_i;
       T *out = static_cast<T *>(prm.o) + (int64_t)b * prm.osb + (int64_t)h * prm.osh + (int64_t)qi * prm.oss;
@@ -311,7 +362,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
 #pragma unroll 1
       for (int c = 0; c < DP / 32; ++c) {
         uint32_t orow[32];
-        ptx::tmem_ld_32x32b_x32(tmem_o + lane_base + (uint32_t)(c * 32), orow);
+        ptx::tmem_ld_32x32b_x32(tmem_o(t) + lane_base + (uint32_t)(c * 32), orow);
         ptx::tmem_ld_wait();
         if (!row_ok) continue;
         const int d0 = c * 32;
@@ -321,10 +372,10 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         if (valid == 32 && prm.osd == 1 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            alignas(16) T pk[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pk[i] = from_f<T>(__uint_as_float(orow[v4 * 8 + i]) * inv);
-            *reinterpret_cast<int4 *>(dst + v4 * 8) = *reinterpret_cast<int4 *>(pk);
+            const float *o4 = reinterpret_cast<const float *>(orow + v4 * 8);
+            const int4 pk = make_int4((int)pack2<T>(o4[0] * inv, o4[1] * inv), (int)pack2<T>(o4[2] * inv, o4[3] * inv),
+                                      (int)pack2<T>(o4[4] * inv, o4[5] * inv), (int)pack2<T>(o4[6] * inv, o4[7] * inv));
+            *reinterpret_cast<int4 *>(dst + v4 * 8) = pk;
           }
         } else {
           for (int i = 0; i < valid; ++i) dst[(int64_t)i * prm.osd] = from_f<T>(__uint_as_float(orow[i]) * inv);
@@ -380,12 +431,12 @@ int try_attention(const AttentionProblem &p, cudaStream_t stream) {
       return kNotEligible;
     Params prm;
     prm.B = (int)p.B; prm.H = (int)p.H; prm.SQ = (int)p.SQ; prm.SK = (int)p.SK; prm.D = (int)p.D;
-    prm.q_tiles = (int)((p.SQ + BM - 1) / BM);
+    prm.q_pairs = (int)((p.SQ + TILES * BM - 1) / (TILES * BM));
     prm.causal = p.causal ? 1 : 0;
     prm.log2e = p.log2e;
     prm.o = p.o;
     prm.osb = p.osb; prm.osh = p.osh; prm.oss = p.oss; prm.osd = p.osd;
-    const int64_t grid = p.B * p.H * prm.q_tiles;
+    const int64_t grid = p.B * p.H * prm.q_pairs;
     if (grid > (1LL << 31) - 1) return kNotEligible;
     if (p.D <= 64) {
       auto kern = attention_kernel<T, 64>;

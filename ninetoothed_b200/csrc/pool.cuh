@@ -91,6 +91,138 @@ max_pool2d_rows_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int
   }
 }
 
+// Fixed-window row-pair path: each lane computes output column q of two
+// consecutive output rows.  All (SH + WH) x WW window loads of the pair are
+// issued up front from clamped (always valid) addresses and the out-of-image
+// ones are replaced by -inf afterwards, so a warp keeps every load in flight at
+// once instead of waiting on them one by one.
+// Grid: x = plane (n, c), y = chunk of 8 row pairs (one per warp), so the
+// only division is one 32-bit n/c split per warp.
+template <typename T, int WH, int WW, int SH, int SW>
+__global__ void __launch_bounds__(256)
+max_pool2d_pairs_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
+                        int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp, int ph,
+                        int pw) {
+  constexpr int NR = SH + WH;  // input rows feeding two output rows
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.y * 8 + (threadIdx.x >> 5);
+  if (pair * 2 < P) {
+    const int p = pair * 2;
+    const unsigned plane_idx = blockIdx.x;
+    const int ci = (int)(plane_idx % (unsigned)C);
+    const int64_t ni = plane_idx / (unsigned)C;
+    const T *plane = in + ni * isn + ci * isc;
+    T *orow = out + ni * osn + ci * osc + p * osp;
+    const int y0 = p * SH - ph;
+    const bool second = p + 1 < P;
+    for (int q = lane; q < Q; q += 32) {
+      const int x0 = q * SW - pw;
+      float v[NR][WW];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const int y = y0 + r;
+        const int yc = min(max(y, 0), H - 1);
+        const T *irow = plane + (int64_t)yc * ish;
+#pragma unroll
+        for (int s2 = 0; s2 < WW; ++s2) {
+          const int xc = min(max(x0 + s2, 0), W - 1);
+          v[r][s2] = to_f(irow[xc]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        const bool y_ok = (unsigned)(y0 + r) < (unsigned)H;
+#pragma unroll
+        for (int s2 = 0; s2 < WW; ++s2) {
+          const bool ok = y_ok && (unsigned)(x0 + s2) < (unsigned)W;
+          v[r][s2] = ok ? v[r][s2] : -INFINITY;
+        }
+      }
+      float m0 = -INFINITY, m1 = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < WH; ++r)
+#pragma unroll
+        for (int s2 = 0; s2 < WW; ++s2) {
+          m0 = v[r][s2] > m0 ? v[r][s2] : m0;
+          m1 = v[r + SH][s2] > m1 ? v[r + SH][s2] : m1;
+        }
+      orow[q] = from_f<T>(m0);
+      if (second) orow[osp + q] = from_f<T>(m1);
+    }
+  }
+}
+
+// 3x3 window, stride 2, padding 1 (the BASELINE pooling after conv2d), 16- or
+// 32-bit elements, even row length, rows starting on a pair boundary.  Lane q
+// loads the element pair (2q, 2q+1) of each input row as one vector and the
+// element 2q-1 as a scalar (an L1 hit: the neighbouring lane's pair), takes the
+// horizontal 3-max in the element type, and the vertical maxima over the 5
+// input rows shared by output rows p and p+1.  The max of elements is exact,
+// so no conversion is needed.
+template <typename T> struct Pair;
+template <> struct Pair<__half> { using V = __half2; };
+template <> struct Pair<__nv_bfloat16> { using V = __nv_bfloat162; };
+template <> struct Pair<float> { using V = float2; };
+
+__device__ __forceinline__ __half vmax(__half a, __half b) { return __hmax(a, b); }
+__device__ __forceinline__ __nv_bfloat16 vmax(__nv_bfloat16 a, __nv_bfloat16 b) { return __hmax(a, b); }
+__device__ __forceinline__ float vmax(float a, float b) { return fmaxf(a, b); }
+template <typename T> __device__ __forceinline__ T neg_inf() { return from_f<T>(-INFINITY); }
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+max_pool2d_3x3s2p1_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
+                          int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp) {
+  using V = typename Pair<T>::V;
+  constexpr int PAIRS = 2;  // row pairs per warp, loaded together
+  const int lane = threadIdx.x & 31;
+  const int first_pair = (blockIdx.y * 8 + (threadIdx.x >> 5)) * PAIRS;
+  if (first_pair * 2 >= P) return;
+  const unsigned plane_idx = blockIdx.x;
+  const int ci = (int)(plane_idx % (unsigned)C);
+  const int64_t ni = plane_idx / (unsigned)C;
+  const T *plane = in + ni * isn + ci * isc;
+  T *oplane = out + ni * osn + ci * osc;
+  const T ninf = neg_inf<T>();
+  for (int q = lane; q < Q; q += 32) {
+    const int x = 2 * q;  // window columns x-1, x, x+1
+    const bool pair_ok = x < W;  // W is even, so x + 1 < W too
+    T hm[PAIRS][5];
+#pragma unroll
+    for (int u = 0; u < PAIRS; ++u) {
+      const int y0 = 4 * (first_pair + u) - 1;  // output rows p = 2 * pair, p + 1
+#pragma unroll
+      for (int r = 0; r < 5; ++r) {
+        const int y = y0 + r;
+        const bool y_ok = (unsigned)y < (unsigned)H;
+        const T *irow = plane + (int64_t)(y_ok ? y : 0) * ish;
+        const V v = *reinterpret_cast<const V *>(irow + (pair_ok ? x : 0));
+        const T left = irow[x > 0 ? x - 1 : 0];
+        // x <= W always (the ABI rejects windows that start past the padded
+        // input), so column x - 1 is inside the row whenever x > 0.
+        T m = pair_ok ? vmax(reinterpret_cast<const T *>(&v)[0], reinterpret_cast<const T *>(&v)[1]) : ninf;
+        m = x > 0 ? vmax(m, left) : m;
+        hm[u][r] = y_ok ? m : ninf;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < PAIRS; ++u) {
+      const int p = 2 * (first_pair + u);
+      if (p < P) oplane[(int64_t)p * osp + q] = vmax(vmax(hm[u][0], hm[u][1]), hm[u][2]);
+      if (p + 1 < P) oplane[(int64_t)(p + 1) * osp + q] = vmax(vmax(hm[u][2], hm[u][3]), hm[u][4]);
+    }
+  }
+}
+
+template <typename T, int WH, int WW, int SH, int SW>
+inline void launch_pairs(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
+                         int64_t P, int64_t Q, const int64_t *os, int64_t ph, int64_t pw, cudaStream_t stream) {
+  const int64_t pair_rows = (P + 1) / 2;
+  const dim3 grid((unsigned)(n * c), (unsigned)((pair_rows + 7) / 8));
+  max_pool2d_pairs_kernel<T, WH, WW, SH, SW><<<grid, 256, 0, stream>>>(
+      in, out, (int)c, (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], (int)ph, (int)pw);
+}
+
 template <typename T, int WH, int WW, int SH, int SW>
 inline void launch_rows(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
                         int64_t P, int64_t Q, const int64_t *os, int64_t wh, int64_t ww, int64_t sh, int64_t sw,
@@ -128,16 +260,25 @@ extern "C" int nt_b200_max_pool2d(const void *input, void *output, int64_t n, in
     // The row path keeps the in-plane offsets (y * row stride + x) in 32 bits.
     const bool int32_ok = h < (1 << 30) && w < (1 << 30) && out_h < (1 << 30) && out_w < (1 << 30) &&
                           c < (1 << 30) && (h + 1) * (is[2] < 0 ? -is[2] : is[2]) < (1LL << 31);
-    if (is[3] == 1 && os[3] == 1 && int32_ok) {
+    const bool grid_ok = n * c < (1LL << 31) && (out_h + 15) / 16 < 65535;
+    if (is[3] == 1 && os[3] == 1 && int32_ok && h > 0 && w > 0 && grid_ok) {
       using T = scalar_t;
       const T *in = static_cast<const T *>(input);
       T *out = static_cast<T *>(output);
-      if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2)
-        nt::pool::launch_rows<T, 3, 3, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, 3, 3, 2, 2, pad_h, pad_w, s);
+      const bool pair_aligned = w % 2 == 0 && is[2] % 2 == 0 && is[1] % 2 == 0 && is[0] % 2 == 0 &&
+                                (reinterpret_cast<uintptr_t>(input) % (2 * sizeof(T))) == 0;
+      if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2 && pad_h == 1 && pad_w == 1 &&
+          pair_aligned) {
+        const dim3 grid((unsigned)(n * c), (unsigned)(((out_h + 1) / 2 + 15) / 16));
+        nt::pool::max_pool2d_3x3s2p1_kernel<T><<<grid, 256, 0, s>>>(in, out, (int)c, (int)h, (int)w, (int)out_h,
+                                                                    (int)out_w, is[0], is[1], is[2], os[0], os[1],
+                                                                    os[2]);
+      } else if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2)
+        nt::pool::launch_pairs<T, 3, 3, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
       else if (window_h == 3 && window_w == 3 && stride_h == 3 && stride_w == 3)
-        nt::pool::launch_rows<T, 3, 3, 3, 3>(in, out, n, c, h, w, is, out_h, out_w, os, 3, 3, 3, 3, pad_h, pad_w, s);
+        nt::pool::launch_pairs<T, 3, 3, 3, 3>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
       else if (window_h == 2 && window_w == 2 && stride_h == 2 && stride_w == 2)
-        nt::pool::launch_rows<T, 2, 2, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, 2, 2, 2, 2, pad_h, pad_w, s);
+        nt::pool::launch_pairs<T, 2, 2, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
       else
         nt::pool::launch_rows<T, 0, 0, 0, 0>(in, out, n, c, h, w, is, out_h, out_w, os, window_h, window_w,
                                               stride_h, stride_w, pad_h, pad_w, s);

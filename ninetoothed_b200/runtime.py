@@ -80,9 +80,11 @@ class Kernel:
         output = values[self.outputs[0]] if self.outputs else None
         if any(values[name].numel() == 0 for name in self.outputs):
             return output
-        with torch.cuda.device(device):
-            stream = torch.cuda.current_stream(device).cuda_stream
-            code = self.launch(values, stream)
+        if device.index == torch.cuda.current_device():
+            code = self.launch(values, torch.cuda.current_stream(device).cuda_stream)
+        else:
+            with torch.cuda.device(device):
+                code = self.launch(values, torch.cuda.current_stream(device).cuda_stream)
         if code != 0:
             raise KernelLaunchError(code)
         return output

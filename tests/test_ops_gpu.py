@@ -171,6 +171,15 @@ def test_max_pool2d_baseline_config_bit_exact():
     )
 
 
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16, torch.float32))
+@pytest.mark.parametrize("ceil_mode", (False, True))
+@pytest.mark.parametrize("hw", ((56, 56), (9, 10), (8, 7)))
+def test_max_pool2d_3x3_s2_p1_edges(dtype, ceil_mode, hw):
+    x = torch.randn((3, 5, *hw), device=DEV).to(dtype)
+    y = programs.max_pool2d(x, (3, 3), ceil_mode=ceil_mode, stride=2, padding=1)
+    assert torch.equal(y, F.max_pool2d(x, 3, 2, 1, ceil_mode=ceil_mode))
+
+
 @pytest.mark.parametrize("name", golden_io.names("max_pool2d_"))
 def test_max_pool2d_golden(name):
     g = golden_io.load(name)
