@@ -53,6 +53,7 @@ enum NtB200DataType {
 #define NT_B200_ERR_SHAPE_MISMATCH 10003   /* output shape inconsistent with inputs */
 #define NT_B200_ERR_NO_DEVICE 10004        /* no sm_100 device current */
 #define NT_B200_ERR_DEVICE_TIMEOUT 10005   /* a bounded device-side wait gave up */
+#define NT_B200_ERR_WORKSPACE_TOO_LARGE 10006 /* staging exceeds the library's fixed array */
 
 /* Library identity and diagnostics. */
 int nt_b200_version(void);
@@ -192,6 +193,27 @@ int nt_b200_conv2d(const void *input, const void *filter, void *output, int64_t 
  */
 int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w,
                                       int64_t k, int64_t r, int64_t s, int dtype);
+
+/*
+ * conv2d exactly as nt_b200_conv2d, for callers that cannot provide device
+ * memory at call time: a C host program without a device allocator, a loop
+ * that must not call cudaMalloc (it synchronises the device and stalls other
+ * streams), or an application whose memory budget is fixed at start-up.  The
+ * NHWC/KRSC staging goes to a 64 MiB array inside the library (held on every
+ * GPU that loads the library until the process exits); the call allocates
+ * nothing.  Problems needing more staging than 64 MiB return
+ * NT_B200_ERR_WORKSPACE_TOO_LARGE without launching.  All calls on a device
+ * share the array, so calls whose kernels overlap on the GPU race; calls on
+ * one stream are safe.  The first call on a device looks the array's address
+ * up with that device current; make it before any stream capture.
+ * No counterpart in the reference.
+ */
+int nt_b200_conv2d_no_alloc(const void *input, const void *filter, void *output,
+                            int64_t n, int64_t c, int64_t h, int64_t w, int64_t k,
+                            int64_t r, int64_t s, int64_t pad_h, int64_t pad_w,
+                            const int64_t *input_strides,
+                            const int64_t *filter_strides,
+                            const int64_t *output_strides, int dtype, void *stream);
 
 #ifdef __cplusplus
 }

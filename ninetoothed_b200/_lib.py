@@ -38,6 +38,7 @@ ERROR_CODES = {
     10003: "NT_B200_ERR_SHAPE_MISMATCH",
     10004: "NT_B200_ERR_NO_DEVICE",
     10005: "NT_B200_ERR_DEVICE_TIMEOUT",
+    10006: "NT_B200_ERR_WORKSPACE_TOO_LARGE",
 }
 
 _P = ctypes.c_void_p
@@ -77,6 +78,10 @@ SIGNATURES = {
         (_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _PI64, _PI64, _PI64, _P, _I, _C, _P),
     ),
     "nt_b200_conv2d_workspace_size": (ctypes.c_int64, (_I, _I, _I, _I, _I, _I, _I, _C)),
+    "nt_b200_conv2d_no_alloc": (
+        ctypes.c_int,
+        (_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _I, _PI64, _PI64, _PI64, _C, _P),
+    ),
 }
 
 _lock = threading.Lock()

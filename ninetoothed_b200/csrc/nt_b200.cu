@@ -8,6 +8,7 @@
 #include "elementwise.cuh"
 #include "pool.cuh"
 #include "contractions.cuh"
+#include "conv_no_alloc.cu"
 
 namespace nt {
 
@@ -49,6 +50,7 @@ extern "C" const char *nt_b200_error_string(int code) {
     case NT_B200_ERR_SHAPE_MISMATCH: return "shape mismatch";
     case NT_B200_ERR_NO_DEVICE: return "no sm_100 device";
     case NT_B200_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+    case NT_B200_ERR_WORKSPACE_TOO_LARGE: return "conv2d staging exceeds the library's fixed 64 MiB array";
     default: return cudaGetErrorString(static_cast<cudaError_t>(code));
   }
 }
