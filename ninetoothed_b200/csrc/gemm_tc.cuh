@@ -423,6 +423,47 @@ nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW
   }
 }
 
+// Contiguous-plane NCHW -> NHWC (each (n, c) plane dense, HW a multiple of 8,
+// 16-byte aligned planes): a 64-channel x 64-pixel tile per CTA moves through
+// shared memory with 16-byte loads along pixels and 16-byte stores along
+// channels, no index division per element.
+template <typename T>
+__global__ void __launch_bounds__(256)
+nchw_to_nhwc_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int64_t isn, int64_t isc) {
+  static_assert(sizeof(T) == 2, "16-bit elements");
+  __shared__ __align__(16) T tile[64][64 + 8];  // [channel][pixel], rows padded by 16 bytes
+  const int n = blockIdx.z, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
+  const int t = threadIdx.x;
+  const T *src = in + (int64_t)n * isn;
+  // load: 64 channels x 8 vectors of 8 pixels
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = t + 256 * i;   // 0..511
+    const int cc = v / 8, pv = v % 8;
+    const int c = c0 + cc, pix = p0 + pv * 8;
+    int4 val = make_int4(0, 0, 0, 0);
+    if (c < C && pix < HW) val = __ldcs(reinterpret_cast<const int4 *>(src + (int64_t)c * isc + pix));
+    *reinterpret_cast<int4 *>(&tile[cc][pv * 8]) = val;
+  }
+  __syncthreads();
+  // store: 64 pixels x 8 vectors of 8 channels; a warp takes 32 consecutive
+  // pixels of one channel group, so its shared-memory reads are one
+  // contiguous 64-byte run per channel
+  T *dst = out + (int64_t)n * HW * C;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = t + 256 * i;
+    const int pp = v % 64, cv = v / 64;
+    const int pix = p0 + pp, c = c0 + cv * 8;
+    if (pix < HW && c < C) {
+      alignas(16) T pk[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pk[e] = tile[cv * 8 + e][pp];
+      *reinterpret_cast<int4 *>(dst + (int64_t)pix * C + c) = *reinterpret_cast<int4 *>(pk);
+    }
+  }
+}
+
 // KCRS filter (any strides) -> dense KRSC.
 template <typename T>
 __global__ void kcrs_to_krsc_kernel(const T *__restrict__ in, T *__restrict__ out, int K, int C, int R, int S,
@@ -472,8 +513,14 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     {
       const int HW = (int)(p.h * p.w);
       dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)p.n);
-      nchw_to_nhwc_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW, (int)p.w,
-                                                       p.is[0], p.is[1], p.is[2], p.is[3]);
+      const bool dense_planes = p.is[3] == 1 && p.is[2] == p.w && HW % 8 == 0 && p.is[1] % 8 == 0 &&
+                                p.is[0] % 8 == 0 && (reinterpret_cast<uintptr_t>(p.input) & 15u) == 0;
+      if (dense_planes)
+        nchw_to_nhwc_vec_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
+                                                             p.is[0], p.is[1]);
+      else
+        nchw_to_nhwc_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
+                                                         (int)p.w, p.is[0], p.is[1], p.is[2], p.is[3]);
       const int64_t total = p.k * p.r * p.s * p.c;
       const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
       kcrs_to_krsc_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T *>(p.filter), flt, (int)p.k, (int)p.c,

@@ -214,6 +214,79 @@ max_pool2d_3x3s2p1_kernel(const T *__restrict__ in, T *__restrict__ out, int C, 
   }
 }
 
+// Vector form of the 3x3 / stride 2 / padding 1 path for 16-bit elements, row
+// length W <= 64 with W % 8 == 0 and Q % 4 == 0 (56 -> 28 in the BASELINE
+// config).  An 8-lane group owns one pair of output rows: lane j loads input
+// columns [8j, 8j + 8) of each of the 5 input rows with one 16-byte load,
+// takes column 8j - 1 from lane j - 1 by a shuffle, and writes output
+// columns [4j, 4j + 4) of both rows with 8-byte stores.  A warp covers 4 row
+// pairs, so 20 16-byte loads per lane group are in flight together.
+template <typename T>
+__global__ void __launch_bounds__(256)
+max_pool2d_3x3s2p1_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
+                              int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp,
+                              int pairs_per_plane, int64_t total_pairs) {
+  const int lane = threadIdx.x & 31;
+  const int j = lane & 7;  // lane within the group
+  const int64_t g = (int64_t)blockIdx.x * 32 + (threadIdx.x >> 3);
+  const bool active = g < total_pairs;
+  const int64_t gg = active ? g : 0;
+  const unsigned plane_idx = (unsigned)(gg / pairs_per_plane);
+  const int pair = (int)(gg - (int64_t)plane_idx * pairs_per_plane);
+  const int ci = (int)(plane_idx % (unsigned)C);
+  const int64_t ni = plane_idx / (unsigned)C;
+  const T *plane = in + ni * isn + ci * isc;
+  const int p = 2 * pair;
+  const int y0 = 2 * p - 1;
+  const bool col_ok = 8 * j < W;
+  const T ninf = neg_inf<T>();
+  T hm[5][4];
+#pragma unroll
+  for (int r = 0; r < 5; ++r) {
+    const int y = y0 + r;
+    const bool y_ok = (unsigned)y < (unsigned)H;
+    const T *irow = plane + (int64_t)(y_ok ? y : 0) * ish;
+    int4 raw = make_int4(0, 0, 0, 0);
+    if (active && col_ok) raw = *reinterpret_cast<const int4 *>(irow + 8 * j);
+    const T *x = reinterpret_cast<const T *>(&raw);
+    // column 8j - 1 is the last element held by lane j - 1 (padding for j = 0)
+    const unsigned short last = reinterpret_cast<const unsigned short *>(&raw)[7];
+    const unsigned short prev_bits = (unsigned short)__shfl_up_sync(0xffffffffu, (unsigned)last, 1, 8);
+    T left;
+    *reinterpret_cast<unsigned short *>(&left) = prev_bits;
+    if (j == 0) left = ninf;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const T l = k == 0 ? left : x[2 * k - 1];
+      const T m = vmax(vmax(l, x[2 * k]), x[2 * k + 1]);
+      hm[r][k] = (y_ok && col_ok) ? m : ninf;
+    }
+  }
+  if (!active || 4 * j >= Q) return;
+  T *orow = out + ni * osn + ci * osc + (int64_t)p * osp + 4 * j;
+  alignas(8) T o0[4], o1[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    o0[k] = vmax(vmax(hm[0][k], hm[1][k]), hm[2][k]);
+    o1[k] = vmax(vmax(hm[2][k], hm[3][k]), hm[4][k]);
+  }
+  *reinterpret_cast<uint2 *>(orow) = *reinterpret_cast<uint2 *>(o0);
+  if (p + 1 < P) *reinterpret_cast<uint2 *>(orow + osp) = *reinterpret_cast<uint2 *>(o1);
+}
+
+template <typename T>
+inline void launch_vec(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
+                       int64_t P, int64_t Q, const int64_t *os, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    const int pairs_per_plane = (int)((P + 1) / 2);
+    const int64_t total_pairs = n * c * pairs_per_plane;
+    const int64_t blocks = (total_pairs + 31) / 32;
+    max_pool2d_3x3s2p1_vec_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(
+        in, out, (int)c, (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], pairs_per_plane,
+        total_pairs);
+  }
+}
+
 template <typename T, int WH, int WW, int SH, int SW>
 inline void launch_pairs(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
                          int64_t P, int64_t Q, const int64_t *os, int64_t ph, int64_t pw, cudaStream_t stream) {
@@ -267,8 +340,14 @@ extern "C" int nt_b200_max_pool2d(const void *input, void *output, int64_t n, in
       T *out = static_cast<T *>(output);
       const bool pair_aligned = w % 2 == 0 && is[2] % 2 == 0 && is[1] % 2 == 0 && is[0] % 2 == 0 &&
                                 (reinterpret_cast<uintptr_t>(input) % (2 * sizeof(T))) == 0;
-      if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2 && pad_h == 1 && pad_w == 1 &&
-          pair_aligned) {
+      const bool vec_ok = sizeof(T) == 2 && w <= 64 && w % 8 == 0 && out_w % 4 == 0 && out_w * 2 <= w + 1 &&
+                          is[2] % 8 == 0 && is[1] % 8 == 0 && is[0] % 8 == 0 && os[2] % 4 == 0 && os[1] % 4 == 0 &&
+                          os[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(input) & 15u) == 0 &&
+                          (reinterpret_cast<uintptr_t>(output) & 7u) == 0;
+      if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2 && pad_h == 1 && pad_w == 1 && vec_ok) {
+        nt::pool::launch_vec<T>(in, out, n, c, h, w, is, out_h, out_w, os, s);
+      } else if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2 && pad_h == 1 && pad_w == 1 &&
+                 pair_aligned) {
         const dim3 grid((unsigned)(n * c), (unsigned)(((out_h + 1) / 2 + 15) / 16));
         nt::pool::max_pool2d_3x3s2p1_kernel<T><<<grid, 256, 0, s>>>(in, out, (int)c, (int)h, (int)w, (int)out_h,
                                                                     (int)out_w, is[0], is[1], is[2], os[0], os[1],
