@@ -7,20 +7,20 @@
 //   o = o * alpha + round(p) v; l = l * alpha + rowsum p   (m = -inf, l = 1 at start)
 //   out = round(o / l)
 //
-// One CTA per (batch, head, 128-query tile); 6 warps:
-//   warp 0     TMA producer: Q once, then K_j and V_j (128 keys each) into a
-//              2-stage ring;
-//   warp 1     allocates TMEM and issues the MMAs from one thread:
-//              S_j = Q K_j^T into one of two TMEM S buffers (128 fp32 columns),
-//              O += P_j V_j into the TMEM O accumulator;
-//   warps 2-5  one thread per query row (= TMEM lane): scale Q in place, read
-//              S_j from TMEM, online softmax in registers, rescale O in TMEM
-//              when the row max moved, write P_j (rounded to the input dtype)
-//              to shared memory in the 128-byte-swizzled K-major layout the
-//              next MMA reads, and finally O / l to global memory.
-// S_{j+1} = Q K_{j+1}^T runs on the tensor cores while the softmax threads work
-// on S_j.  Causal tiles skip key blocks above the diagonal and are scheduled
-// longest first.  Every mbarrier wait is bounded in time.
+// One CTA per (batch, head, 256 queries) = two 128-row Q tiles; 10 warps:
+//   warp 0     TMA producer: both Q tiles once, then K_j and V_j (128 keys
+//              each) through a 5-slot shared-memory ring;
+//   warp 1     allocates TMEM and issues the MMAs from one thread, tile by
+//              tile: S_t = Q_t K_j^T into tile t's S columns, then
+//              O_t += P_t V_j with P_t read from tensor memory;
+//   warps 2-5, 6-9  one warpgroup per Q tile, one thread per query row (= TMEM
+//              lane): scale Q in place, read S from TMEM, online softmax in
+//              registers, rescale O in TMEM when the row max moved far enough,
+//              write P (rounded to the input dtype, two per 32-bit column)
+//              over S's columns, and finally O / l to global memory.
+// While one tile's softmax runs, the tensor cores work on the other tile.
+// Causal tiles skip key blocks above the diagonal and are scheduled longest
+// first.  Every mbarrier wait is bounded in time.
 #pragma once
 
 #include <cuda.h>
@@ -45,7 +45,7 @@ namespace attn {
 constexpr int BM = 128;     // queries per Q tile
 constexpr int BN = 128;     // keys per block
 constexpr int TILES = 2;    // Q tiles per CTA, one softmax warpgroup each
-constexpr int RING = 3;     // K/V shared-memory slots (K_j, V_j, K_j+1, ... in load order)
+constexpr int RING = 5;     // K/V shared-memory slots (K_j, V_j, K_j+1, ... in load order)
 constexpr int THREADS = 64 + TILES * 128;
 constexpr int TMEM_COLS = 512;
 // A row's running max is only moved when a block's max exceeds it by more
@@ -59,11 +59,9 @@ struct Layout {
   static constexpr int ATOMS = DP / 64;                // 128-byte swizzle atoms along head_dim
   static constexpr int Q_BYTES = BM * DP * 2;          // one Q tile
   static constexpr int KV_BYTES = BN * DP * 2;         // one K or V block
-  static constexpr int P_BYTES = BM * BN * 2;          // one P tile
   static constexpr int Q_OFF = 0;
   static constexpr int RING_OFF = Q_OFF + TILES * Q_BYTES;
-  static constexpr int P_OFF = RING_OFF + RING * KV_BYTES;
-  static constexpr int CTRL_OFF = P_OFF + TILES * P_BYTES;
+  static constexpr int CTRL_OFF = RING_OFF + RING * KV_BYTES;
   static constexpr int SMEM_BYTES = CTRL_OFF + 256 + 1024;
 };
 
@@ -105,12 +103,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
   // barrier slots (8 bytes each)
   const uint32_t q_full = ctrl + 0, q_ready = ctrl + 8;
   auto slot_full = [&](int s) { return ctrl + 16 + 8u * s; };
-  auto slot_empty = [&](int s) { return ctrl + 40 + 8u * s; };
-  auto s_full = [&](int t) { return ctrl + 64 + 8u * t; };
-  auto p_full = [&](int t) { return ctrl + 80 + 8u * t; };
-  auto o_done = [&](int t) { return ctrl + 96 + 8u * t; };
-  volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(smem + L::CTRL_OFF + 128);
-  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::CTRL_OFF + 132);
+  auto slot_empty = [&](int s) { return ctrl + 56 + 8u * s; };
+  auto s_full = [&](int t) { return ctrl + 96 + 8u * t; };
+  auto p_full = [&](int t) { return ctrl + 112 + 8u * t; };
+  auto o_done = [&](int t) { return ctrl + 128 + 8u * t; };
+  volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(smem + L::CTRL_OFF + 160);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::CTRL_OFF + 164);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -203,12 +201,12 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
         const uint32_t vb = slot_addr(2 * j + 1);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t poff = (kk / 4) * (BM * 128) + (kk % 4) * 32;
-          const uint64_t a_desc = ptx::sw128_desc(base + L::P_OFF + t * L::P_BYTES + poff, 16, 1024);
+          // P_t: 128 keys packed two per column in tile t's S columns
           const uint64_t b_desc = ptx::sw128_desc(vb + kk * 16 * 128, BN * 128, 1024);
-          ptx::mma_f16_ss(tmem_o(t), a_desc, b_desc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          ptx::mma_f16_ts(tmem_o(t), tmem_s(t) + (uint32_t)(kk * 8), b_desc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit(o_done(t));
+        // O_t is read by the softmax warps only after the last block
+        if (j == n_blk[t] - 1) ptx::mma_commit(o_done(t));
       };
       bool ok = ptx::mbar_wait(q_ready, 0, abort_flag) && wait_item(0);
       if (ok) {
@@ -269,7 +267,6 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     ptx::mbar_arrive(q_ready);
 
     float m_i = -INFINITY, l_i = 1.f;
-    uint8_t *p_tile = smem + L::P_OFF + t * L::P_BYTES;
     for (int j = 0; j < n_t && ok; ++j) {
       if (!ptx::mbar_wait_warp(s_full(t), (uint32_t)j & 1u, abort_flag)) { ok = false; break; }
       ptx::tc_fence_after();
@@ -314,47 +311,38 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
 #pragma unroll
         for (int v = 0; v < u; ++v) lp[v] += lp[v + u];
       const float l_blk = lp[0];
-      // O_t must hold P(j-1) V(j-1) before it is rescaled, and P_t's buffer
-      // must be free before it is rewritten.
-      if (j > 0) {
-        if (!ptx::mbar_wait_warp(o_done(t), (uint32_t)(j - 1) & 1u, abort_flag)) { ok = false; break; }
-        ptx::tc_fence_after();
-        if (__any_sync(0xffffffffu, move)) {
+      // O_t holds P(j-1) V(j-1) already: the commit that signalled S_t(j) came
+      // after that MMA, and a commit covers every earlier MMA of its thread.
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
 #pragma unroll 1
-          for (int c = 0; c < DP / 32; ++c) {
-            uint32_t orow[32];
-            const uint32_t taddr = tmem_o(t) + lane_base + (uint32_t)(c * 32);
-            ptx::tmem_ld_32x32b_x32(taddr, orow);
-            ptx::tmem_ld_wait();
+        for (int c = 0; c < DP / 32; ++c) {
+          uint32_t orow[32];
+          const uint32_t taddr = tmem_o(t) + lane_base + (uint32_t)(c * 32);
+          ptx::tmem_ld_32x32b_x32(taddr, orow);
+          ptx::tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            ptx::tmem_st_32x32b_x32(taddr, orow);
-          }
-          ptx::tmem_st_wait();
+          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+          ptx::tmem_st_32x32b_x32(taddr, orow);
         }
       }
       m_i = m_new;
       l_i = l_i * alpha + l_blk;
-      // P row -> shared memory, K-major with 128-byte swizzle: atom a holds keys
-      // [64a, 64a + 64); 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+      // P row -> TMEM over this tile's S columns: column c holds keys 2c (low
+      // half) and 2c + 1, the A-operand layout of the PV MMA.
 #pragma unroll
-      for (int a = 0; a < BN / 64; ++a) {
-        uint8_t *rowp = p_tile + a * (BM * 128) + row * 128;
+      for (int h2 = 0; h2 < BN / 64; ++h2) {
+        uint32_t packed[32];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const float *e = sv + a * 64 + c * 8;
-          const int4 pk = make_int4((int)pack2<T>(e[0], e[1]), (int)pack2<T>(e[2], e[3]), (int)pack2<T>(e[4], e[5]),
-                                    (int)pack2<T>(e[6], e[7]));
-          *reinterpret_cast<int4 *>(rowp + ((c ^ (row & 7)) * 16)) = pk;
-        }
+        for (int i = 0; i < 32; ++i) packed[i] = pack2<T>(sv[h2 * 64 + 2 * i], sv[h2 * 64 + 2 * i + 1]);
+        ptx::tmem_st_32x32b_x32(tmem_s(t) + lane_base + (uint32_t)(h2 * 32), packed);
       }
-      ptx::fence_proxy_async_smem();
+      ptx::tmem_st_wait();
       ptx::tc_fence_before();
       ptx::mbar_arrive(p_full(t));
     }
 
     // epilogue: O / l -> global
-    if (ok && n_t > 0 && ptx::mbar_wait_warp(o_done(t), (uint32_t)(n_t - 1) & 1u, abort_flag)) {
+    if (ok && n_t > 0 && ptx::mbar_wait_warp(o_done(t), 0, abort_flag)) {
       ptx::tc_fence_after();
       const float inv = 1.f / l_i;
       T *out = static_cast<T *>(prm.o) + (int64_t)b * prm.osb + (int64_t)h * prm.osh + (int64_t)qi * prm.oss;

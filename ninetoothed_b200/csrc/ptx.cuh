@@ -143,6 +143,18 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::f16: A is read from tensor memory
+// (lane = row, each 32-bit column holds two consecutive K elements, low half
+// first), K = 16 elements = 8 columns per instruction.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrives on the mbarrier once all previously issued tcgen05.mma of this
 // thread have completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
