@@ -49,10 +49,14 @@ constexpr int RING = 5;     // K/V shared-memory slots (K_j, V_j, K_j+1, ... in 
 constexpr int THREADS = 64 + TILES * 128;
 constexpr int TMEM_COLS = 512;
 // A row's running max is only moved when a block's max exceeds it by more
-// than 2^8 (log2 domain); otherwise p = exp2(s - m) <= 256 against the stale
-// max.  o / l is unchanged mathematically, and O is rescaled in TMEM far less
-// often.
-constexpr float kRescaleThreshold = 8.0f;
+// than 2^kRescaleLog2<T> (log2 domain); otherwise p = exp2(s - m) is taken
+// against the stale max, so p <= 2^kRescaleLog2 -- within float16's range
+// (2^14 < 65504) and far inside bfloat16's.  o / l is unchanged mathematically,
+// the relative precision of p is the same at any scale, and O is rescaled in
+// TMEM only on the rare large jumps.
+template <typename T> struct RescaleLog2;
+template <> struct RescaleLog2<__half> { static constexpr float value = 14.f; };
+template <> struct RescaleLog2<__nv_bfloat16> { static constexpr float value = 24.f; };
 
 template <int DP>  // head_dim padded to 64 or 128
 struct Layout {
@@ -297,14 +301,27 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
 #pragma unroll
         for (int v = 0; v < u; ++v) mp[v] = fmaxf(mp[v], mp[v + u]);
       const float m_blk = mp[0];
-      const bool move = m_blk > m_i + kRescaleThreshold;  // true on the first block (m_i = -inf)
+      const bool move = m_blk > m_i + RescaleLog2<T>::value;  // true on the first block (m_i = -inf)
       const float m_new = move ? m_blk : m_i;
       const float alpha = move ? ex2(m_i - m_new) : 1.f;
+      // p = exp2(s - m) in two halves of 64 keys; each half is packed (two keys
+      // per 32-bit column) and stored over this tile's S columns as soon as it
+      // is done, so the first store's latency overlaps the second half's
+      // exponentials.  Column c holds keys 2c (low half) and 2c + 1: the
+      // A-operand layout of the PV MMA.
       float lp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        sv[c] = ex2(sv[c] - m_new);
-        lp[c & 7] += sv[c];
+      for (int h2 = 0; h2 < BN / 64; ++h2) {
+        uint32_t packed[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int c = h2 * 64 + 2 * i;
+          const float p0 = ex2(sv[c] - m_new), p1 = ex2(sv[c + 1] - m_new);
+          lp[(2 * i) & 7] += p0;
+          lp[(2 * i + 1) & 7] += p1;
+          packed[i] = pack2<T>(p0, p1);
+        }
+        ptx::tmem_st_32x32b_x32(tmem_s(t) + lane_base + (uint32_t)(h2 * 32), packed);
       }
 #pragma unroll
       for (int u = 4; u > 0; u >>= 1)
@@ -313,29 +330,24 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
       const float l_blk = lp[0];
       // O_t holds P(j-1) V(j-1) already: the commit that signalled S_t(j) came
       // after that MMA, and a commit covers every earlier MMA of its thread.
+      // The rescale reuses the registers S held; it must land before the PV MMA
+      // of this block, which waits for p_full below.
       if (j > 0 && __any_sync(0xffffffffu, move)) {
-#pragma unroll 1
-        for (int c = 0; c < DP / 32; ++c) {
-          uint32_t orow[32];
-          const uint32_t taddr = tmem_o(t) + lane_base + (uint32_t)(c * 32);
-          ptx::tmem_ld_32x32b_x32(taddr, orow);
-          ptx::tmem_ld_wait();
+        uint32_t orow[DP];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-          ptx::tmem_st_32x32b_x32(taddr, orow);
-        }
+        for (int c = 0; c < DP / 32; ++c)
+          ptx::tmem_ld_32x32b_x32(tmem_o(t) + lane_base + (uint32_t)(c * 32),
+                                  *reinterpret_cast<uint32_t(*)[32]>(&orow[c * 32]));
+        ptx::tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < DP; ++i) orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+#pragma unroll
+        for (int c = 0; c < DP / 32; ++c)
+          ptx::tmem_st_32x32b_x32(tmem_o(t) + lane_base + (uint32_t)(c * 32),
+                                  *reinterpret_cast<uint32_t(*)[32]>(&orow[c * 32]));
       }
       m_i = m_new;
       l_i = l_i * alpha + l_blk;
-      // P row -> TMEM over this tile's S columns: column c holds keys 2c (low
-      // half) and 2c + 1, the A-operand layout of the PV MMA.
-#pragma unroll
-      for (int h2 = 0; h2 < BN / 64; ++h2) {
-        uint32_t packed[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) packed[i] = pack2<T>(sv[h2 * 64 + 2 * i], sv[h2 * 64 + 2 * i + 1]);
-        ptx::tmem_st_32x32b_x32(tmem_s(t) + lane_base + (uint32_t)(h2 * 32), packed);
-      }
       ptx::tmem_st_wait();
       ptx::tc_fence_before();
       ptx::mbar_arrive(p_full(t));
