@@ -303,8 +303,10 @@ def bench_ops(which, steps, dist, peaks):
             achieved = work / (ms * 1e-3) / 1e12
         else:
             achieved = work / (ms * 1e-3) / 1e9
+        profile = {"addmm": "gemm", "matmul": "gemm", "attention": "attention", "conv2d": "conv2d",
+                   "max_pool2d": "max_pool2d"}[name.split("_bf16")[0].split("_fp16")[0]]
         results[name] = {"value": achieved * dist.world, "per_gpu": achieved, "unit": unit, "ms": ms,
-                         "frac": achieved / peak}
+                         "frac": achieved / peak, "peak": peak, "traffic": profile_traffic(profile)}
 
     s = 8192
     if "addmm" in which or "matmul" in which:
