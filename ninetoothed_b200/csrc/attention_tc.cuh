@@ -116,10 +116,13 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // Work item (batch, head, pair of Q tiles); causal pairs run longest first.
+  // Work item (batch, head, pair of Q tiles).  Causal: the pair index is the
+  // slow coordinate, last (longest) pairs of every head first, so the CTAs
+  // dispatched together have similar lengths and the short ones fill the tail.
   const int per_head = prm.q_pairs;
-  const int bh = blockIdx.x / per_head;
-  const int qp = prm.causal ? per_head - 1 - (int)(blockIdx.x % per_head) : (int)(blockIdx.x % per_head);
+  const int heads = prm.B * prm.H;
+  const int bh = prm.causal ? (int)(blockIdx.x % heads) : (int)(blockIdx.x / per_head);
+  const int qp = prm.causal ? per_head - 1 - (int)(blockIdx.x / heads) : (int)(blockIdx.x % per_head);
   const int b = bh / prm.H, h = bh % prm.H;
   const int q0 = qp * (TILES * BM);
   const int kv_blocks = (prm.SK + BN - 1) / BN;
