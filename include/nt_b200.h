@@ -30,7 +30,9 @@
 extern "C" {
 #endif
 
-/* Element types: the NineToothedDataType values of the reference ABI. */
+/* Element types: the NineToothedDataType values of the reference ABI (0-11),
+ * extended with the two 8-bit float types the reference's matmul/addmm tests
+ * use (torch.float8_e4m3fn, torch.float8_e5m2), which its C++ ABI enum lacks. */
 enum NtB200DataType {
     NT_B200_INT8 = 0,
     NT_B200_INT16 = 1,
@@ -43,7 +45,9 @@ enum NtB200DataType {
     NT_B200_FLOAT16 = 8,
     NT_B200_BFLOAT16 = 9,
     NT_B200_FLOAT32 = 10,
-    NT_B200_FLOAT64 = 11
+    NT_B200_FLOAT64 = 11,
+    NT_B200_FLOAT8_E4M3FN = 12,
+    NT_B200_FLOAT8_E5M2 = 13
 };
 
 /* Host-side argument errors (no launch happened).  Values are above the
@@ -127,8 +131,9 @@ int nt_b200_max_pool2d(const void *input, void *output, int64_t n, int64_t c,
  * output[M,N] = cast_out(cast_f16(sum_k lhs[m,k] * rhs[k,n])) with an fp32
  * accumulator: the `matmul` application (tests/test_matmul.py:41-47) rounds the
  * accumulator to float16 before the store converts it to the output dtype.
- * in_dtype: FLOAT16 or BFLOAT16 (both operands); out_dtype: FLOAT16, BFLOAT16,
- * FLOAT32.  Strides are element strides (row, col) of each 2-D operand.
+ * in_dtype: FLOAT16, BFLOAT16, FLOAT8_E4M3FN or FLOAT8_E5M2 (both operands;
+ * 8-bit operands run on tcgen05 kind::f8f6f4) or FLOAT32 (exact fp32 on CUDA
+ * cores); out_dtype: FLOAT16, BFLOAT16, FLOAT32.  Strides are element strides (row, col) of each 2-D operand.
  */
 int nt_b200_matmul(const void *lhs, const void *rhs, void *output, int64_t m,
                    int64_t n, int64_t k, int64_t lhs_stride_row,
@@ -160,7 +165,8 @@ int nt_b200_addmm(const void *input, const void *mat1, const void *mat2, float b
  * seq_kv masked, optional causal mask (query index >= key index), base-2 online
  * softmax with fp32 running max/sum, p rounded to the input dtype before p @ v,
  * o = acc / l.  Tensors are [batch, heads, seq, head_dim]; strides are 4-entry
- * element-stride arrays.  dtype: FLOAT16 or BFLOAT16 (q, k, v and o).
+ * element-stride arrays.  dtype: FLOAT16 or BFLOAT16 (q, k, v and o; tcgen05) or
+ * FLOAT32 (CUDA cores).
  */
 int nt_b200_attention(const void *q, const void *k, const void *v, int is_causal,
                       void *o, int64_t batch, int64_t heads, int64_t seq_q,

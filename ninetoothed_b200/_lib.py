@@ -30,6 +30,9 @@ DTYPE_CODES = {
     "bfloat16": 9,
     "float32": 10,
     "float64": 11,
+    # extension: the 8-bit float types of the reference's matmul/addmm tests
+    "float8_e4m3fn": 12,
+    "float8_e5m2": 13,
 }
 
 ERROR_CODES = {

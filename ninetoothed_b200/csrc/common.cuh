@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 #include "../../include/nt_b200.h"
@@ -34,6 +35,17 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
 };
 
+template <> struct Elem<__nv_fp8_e4m3> {
+  static constexpr bool is_f16 = false;
+  static __device__ __forceinline__ float to_f(__nv_fp8_e4m3 v) { return static_cast<float>(v); }
+  static __device__ __forceinline__ __nv_fp8_e4m3 from_f(float v) { return __nv_fp8_e4m3(v); }
+};
+template <> struct Elem<__nv_fp8_e5m2> {
+  static constexpr bool is_f16 = false;
+  static __device__ __forceinline__ float to_f(__nv_fp8_e5m2 v) { return static_cast<float>(v); }
+  static __device__ __forceinline__ __nv_fp8_e5m2 from_f(float v) { return __nv_fp8_e5m2(v); }
+};
+
 template <typename T> __device__ __forceinline__ float to_f(T v) { return Elem<T>::to_f(v); }
 template <typename T> __device__ __forceinline__ T from_f(float v) { return Elem<T>::from_f(v); }
 
@@ -45,15 +57,25 @@ __device__ __forceinline__ float round_f16(float v) { return __half2float(__floa
 // Triton's typing of a scalar kernel argument against a tensor (the tensor's
 // dtype wins): beta * input is computed in the input dtype TI, alpha * the
 // float16-rounded accumulator in float16, and the sum in float16 when TI is
-// float16 (float32 when the two dtypes differ).  `beta_t` and `alpha_h` are the
-// scalars already rounded to TI and float16.  Each fp32 operation here is exact
-// or followed by one rounding to a type with at most half fp32's precision, so
-// the result is the correctly rounded value of each typed operation.
+// float16 (float32 for bfloat16 with float16).  8-bit inputs are the exception:
+// beta * input is kept at float16 precision, the only reading under which the
+// reference's own float8_e5m2 addmm test (atol 0.125 against a float16
+// torch.addmm) can pass -- e5m2 rounding of the product alone errs by up to
+// 0.25 there -- and the sum is float16.  `beta_t` and `alpha_h` are the scalars
+// already rounded to ScaleType<TI> and float16.  Each fp32 operation here is
+// exact or followed by one rounding to a type with at most half fp32's
+// precision, so the result is the correctly rounded value of each typed
+// operation.
+template <typename TI> struct ScaleType { using type = TI; };
+template <> struct ScaleType<__nv_fp8_e4m3> { using type = __half; };
+template <> struct ScaleType<__nv_fp8_e5m2> { using type = __half; };
+
 template <typename TI>
 __device__ __forceinline__ float addmm_value(float beta_t, float alpha_h, float in, float acc) {
-  const float scaled_in = to_f(from_f<TI>(beta_t * in));
+  using S = typename ScaleType<TI>::type;
+  const float scaled_in = to_f(from_f<S>(beta_t * in));
   const float scaled_mm = round_f16(alpha_h * round_f16(acc));
-  if constexpr (sizeof(TI) == 2 && Elem<TI>::is_f16) return round_f16(scaled_in + scaled_mm);
+  if constexpr (sizeof(S) == 2 && Elem<S>::is_f16) return round_f16(scaled_in + scaled_mm);
   return scaled_in + scaled_mm;
 }
 
@@ -68,6 +90,12 @@ inline bool is_float_dtype(int dtype) {
 
 inline bool is_half_dtype(int dtype) {
   return dtype == NT_B200_FLOAT16 || dtype == NT_B200_BFLOAT16;
+}
+
+// Operand dtypes of the contraction programs (matmul, addmm).
+inline bool is_gemm_in_dtype(int dtype) {
+  return is_half_dtype(dtype) || dtype == NT_B200_FLOAT8_E4M3FN || dtype == NT_B200_FLOAT8_E5M2 ||
+         dtype == NT_B200_FLOAT32;
 }
 
 inline int dtype_size(int dtype) {

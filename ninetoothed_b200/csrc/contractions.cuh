@@ -45,6 +45,9 @@ int dispatch_in_out(int in_dtype, int out_dtype, F &&f) {
   switch (in_dtype) {
     case NT_B200_FLOAT16: return with_out(__half{});
     case NT_B200_BFLOAT16: return with_out(__nv_bfloat16{});
+    case NT_B200_FLOAT8_E4M3FN: return with_out(__nv_fp8_e4m3{});
+    case NT_B200_FLOAT8_E5M2: return with_out(__nv_fp8_e5m2{});
+    case NT_B200_FLOAT32: return with_out(float{});  // exact fp32 on the CUDA-core path
     default: return NT_B200_ERR_UNSUPPORTED_DTYPE;
   }
 }
@@ -56,7 +59,7 @@ extern "C" int nt_b200_matmul(const void *lhs, const void *rhs, void *output, in
                               int64_t rhs_stride_col, int64_t output_stride_row, int64_t output_stride_col,
                               int in_dtype, int out_dtype, void *stream) {
   if (m < 0 || n < 0 || k < 0) return NT_B200_ERR_INVALID_ARGUMENT;
-  if (!nt::is_half_dtype(in_dtype) || !nt::is_float_dtype(out_dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
+  if (!nt::is_gemm_in_dtype(in_dtype) || !nt::is_float_dtype(out_dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
   if (m == 0 || n == 0) return 0;
   if (!output || (k > 0 && (!lhs || !rhs))) return NT_B200_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -79,7 +82,7 @@ extern "C" int nt_b200_addmm(const void *input, const void *mat1, const void *ma
                              int64_t mat2_stride_row, int64_t mat2_stride_col, int64_t output_stride_row,
                              int64_t output_stride_col, int in_dtype, int out_dtype, void *stream) {
   if (m < 0 || n < 0 || k < 0) return NT_B200_ERR_INVALID_ARGUMENT;
-  if (!nt::is_half_dtype(in_dtype) || !nt::is_float_dtype(out_dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
+  if (!nt::is_gemm_in_dtype(in_dtype) || !nt::is_float_dtype(out_dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
   if (m == 0 || n == 0) return 0;
   if (!output || !input || (k > 0 && (!mat1 || !mat2))) return NT_B200_ERR_INVALID_ARGUMENT;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -88,7 +91,7 @@ extern "C" int nt_b200_addmm(const void *input, const void *mat1, const void *ma
     using TO = decltype(to);
     // Scalars take the dtype of the tensor they multiply (Triton's typing of a
     // scalar argument against a tensor): beta -> TI, alpha -> float16.
-    const float beta_t = static_cast<float>(TI(beta));
+    const float beta_t = static_cast<float>(typename nt::ScaleType<TI>::type(beta));
     const float alpha_h = static_cast<float>(__half(alpha));
     beta = beta_t;
     alpha = alpha_h;
@@ -146,7 +149,7 @@ extern "C" int nt_b200_attention(const void *q, const void *k, const void *v, in
                                  const int64_t *o_strides, int dtype, void *stream) {
   if (batch < 0 || heads < 0 || seq_q < 0 || seq_kv < 0 || head_dim < 0) return NT_B200_ERR_INVALID_ARGUMENT;
   if (head_dim > 128) return NT_B200_ERR_INVALID_ARGUMENT;  // the reference's upper_bound=128 on head_dim
-  if (!nt::is_half_dtype(dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
+  if (!nt::is_float_dtype(dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;  // fp32: CUDA-core path
   if (batch * heads * seq_q * head_dim == 0) return 0;
   if (seq_kv == 0) return NT_B200_ERR_INVALID_ARGUMENT;
   if (!q || !k || !v || !o || !q_strides || !k_strides || !v_strides || !o_strides)

@@ -17,6 +17,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp8.h>
 #include "common.cuh"
 #include "ptx.cuh"
 
@@ -68,18 +69,26 @@ template <typename T> constexpr CUtensorMapDataType tmap_dtype();
 template <> constexpr CUtensorMapDataType tmap_dtype<__half>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT16; }
 template <> constexpr CUtensorMapDataType tmap_dtype<__nv_bfloat16>() { return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; }
 template <> constexpr CUtensorMapDataType tmap_dtype<float>() { return CU_TENSOR_MAP_DATA_TYPE_FLOAT32; }
+template <> constexpr CUtensorMapDataType tmap_dtype<__nv_fp8_e4m3>() { return CU_TENSOR_MAP_DATA_TYPE_UINT8; }
+template <> constexpr CUtensorMapDataType tmap_dtype<__nv_fp8_e5m2>() { return CU_TENSOR_MAP_DATA_TYPE_UINT8; }
 
 template <typename T> __host__ __device__ constexpr uint32_t umma_format();
 template <> __host__ __device__ constexpr uint32_t umma_format<__half>() { return 0; }
 template <> __host__ __device__ constexpr uint32_t umma_format<__nv_bfloat16>() { return 1; }
 template <> __host__ __device__ constexpr uint32_t umma_format<float>() { return 0; }
+template <> __host__ __device__ constexpr uint32_t umma_format<__nv_fp8_e4m3>() { return 0; }
+template <> __host__ __device__ constexpr uint32_t umma_format<__nv_fp8_e5m2>() { return 1; }
 
 // ------------------------------------------------------------------ kernel
 namespace gemm {
 
 constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, GROUP_M = 16;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE_BYTES = BK * BN * 2;  // 32 KB
+constexpr int A_STAGE_BYTES = BM * 128;  // 16 KB: 128 rows of one 128-byte swizzle row
+constexpr int B_STAGE_BYTES = BN * 128;  // 32 KB
+// A k-block is one 128-byte row of K elements: 64 for 16-bit, 128 for 8-bit
+// types; one MMA instruction consumes 32 bytes of K (16 or 32 elements).
+template <typename T> __host__ __device__ constexpr int kblock() { return 128 / (int)sizeof(T); }
+template <typename T> __host__ __device__ constexpr int mma_k() { return 32 / (int)sizeof(T); }
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
@@ -202,7 +211,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
-          const int k0 = kb * BK;
+          const int k0 = kb * kblock<TI>();
           if constexpr (EPI == Epilogue::kConv) {
             // A: BP x BQ pixels x 64 channels of the NHWC input at filter tap
             // (r, s); coordinates outside the image read as zero (the padding).
@@ -218,8 +227,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           ptx::tma_load_2d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, k0, m0);
           if constexpr (B_MN_MAJOR) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES + j * (BK * 128), &tmap_b, fb, n0 + 64 * j, k0);
+            for (int j = 0; j < BN / kblock<TI>(); ++j)
+              ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES + j * (kblock<TI>() * 128), &tmap_b, fb,
+                               n0 + kblock<TI>() * j, k0);
           } else {
             ptx::tma_load_2d(b_base + stage * B_STAGE_BYTES, &tmap_b, fb, k0, n0);
           }
@@ -231,7 +241,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = ptx::f16_idesc(umma_format<TI>(), 0, B_MN_MAJOR ? 1 : 0, BM, BN);
+      constexpr uint32_t idesc = ptx::f16_idesc(umma_format<TI>(), 0, B_MN_MAJOR ? 1 : 0, BM, BN);  // same
+      // bit layout for kind::f8f6f4 (format codes E4M3 = 0, E5M2 = 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -248,14 +259,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           const uint32_t a_addr = a_base + stage * A_STAGE_BYTES;
           const uint32_t b_addr = b_base + stage * B_STAGE_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K
             const uint64_t a_desc = ptx::sw128_desc(a_addr + kk * 32, 16, 1024);
             uint64_t b_desc;
             if constexpr (B_MN_MAJOR)
-              b_desc = ptx::sw128_desc(b_addr + kk * 16 * 128, BK * 128, 1024);
+              b_desc = ptx::sw128_desc(b_addr + kk * mma_k<TI>() * 128, kblock<TI>() * 128, 1024);
             else
               b_desc = ptx::sw128_desc(b_addr + kk * 32, 16, 1024);
-            ptx::mma_f16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            if constexpr (sizeof(TI) == 1)
+              ptx::mma_f8_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              ptx::mma_f16_ss(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           ptx::mma_commit(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -349,41 +363,43 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 // returns kNotEligible otherwise so the caller takes the general-layout path.
 template <typename TI, typename TO, Epilogue EPI>
 int try_gemm(const GemmProblem &p, cudaStream_t stream) {
-  if constexpr (sizeof(TI) != 2) {
+  if constexpr (sizeof(TI) > 2) {
     return kNotEligible;
   } else {
     using namespace gemm;
+    constexpr int E = (int)sizeof(TI);
+    constexpr int KB = kblock<TI>();
     if (p.K <= 0) return kNotEligible;
     if (p.M > (1LL << 31) - 1 || p.N > (1LL << 31) - 1 || p.K > (1LL << 31) - 1) return kNotEligible;
     // A must be K-contiguous with 16-byte aligned rows (TMA rules).
     const auto aligned16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-    if (p.sak != 1 || (p.sam * 2) % 16 != 0 || !aligned16(p.a)) return kNotEligible;
+    if (p.sak != 1 || (p.sam * E) % 16 != 0 || !aligned16(p.a)) return kNotEligible;
     if (p.M > 1 && p.sam < p.K) return kNotEligible;
     bool b_mn;
-    if (p.sbn == 1 && (p.sbk * 2) % 16 == 0 && (p.K == 1 || p.sbk >= p.N)) b_mn = true;
-    else if (p.sbk == 1 && (p.sbn * 2) % 16 == 0 && (p.N == 1 || p.sbn >= p.K)) b_mn = false;
+    if (p.sbn == 1 && (p.sbk * E) % 16 == 0 && (p.K == 1 || p.sbk >= p.N)) b_mn = true;
+    else if (p.sbk == 1 && (p.sbn * E) % 16 == 0 && (p.N == 1 || p.sbn >= p.K)) b_mn = false;
     else return kNotEligible;
     if (!aligned16(p.b)) return kNotEligible;
-    if (p.K * 2 < 16 || (!b_mn && p.K * 2 < 16) || (b_mn && p.N * 2 < 16)) return kNotEligible;
+    if (p.K * E < 16 || (b_mn && p.N * E < 16)) return kNotEligible;
 
     CUtensorMap ta, tb;
-    if (!make_tmap_2d(&ta, p.a, tmap_dtype<TI>(), 2, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.sam, BK, BM))
+    if (!make_tmap_2d(&ta, p.a, tmap_dtype<TI>(), E, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.sam, KB, BM))
       return kNotEligible;
     if (b_mn) {
-      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), 2, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.sbk, 64, BK))
+      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), E, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.sbk, KB, KB))
         return kNotEligible;
     } else {
-      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), 2, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.sbn, BK, BN))
+      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), E, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.sbn, KB, BN))
         return kNotEligible;
     }
-    Params prm;
+    Params prm{};
     prm.M = p.M; prm.N = p.N; prm.K = p.K;
     prm.out = p.out; prm.som = p.som; prm.son = p.son;
     prm.bias = p.bias; prm.sim = p.sim; prm.sin = p.sin;
     prm.beta = p.beta; prm.alpha = p.alpha;
     prm.tiles_m = (int)((p.M + BM - 1) / BM);
     prm.tiles_n = (int)((p.N + BN - 1) / BN);
-    prm.num_kb = (int)((p.K + BK - 1) / BK);
+    prm.num_kb = (int)((p.K + KB - 1) / KB);
     const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
     if (tiles > (1LL << 30)) return kNotEligible;
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());

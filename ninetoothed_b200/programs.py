@@ -16,6 +16,7 @@ import torch
 from ninetoothed_b200 import _lib
 from ninetoothed_b200.runtime import (
     FLOAT_DTYPES,
+    GEMM_DTYPES,
     HALF_DTYPES,
     Kernel,
     KernelLaunchError,
@@ -48,7 +49,7 @@ def _launch_matmul(v, stream):
 # tests/test_matmul.py:14-47: arrangement(lhs, rhs, output) + application.
 matmul_kernel = Kernel(
     name="matmul",
-    args=(TensorArg("lhs", 2, HALF_DTYPES), TensorArg("rhs", 2, HALF_DTYPES), TensorArg("output", 2)),
+    args=(TensorArg("lhs", 2, GEMM_DTYPES), TensorArg("rhs", 2, GEMM_DTYPES), TensorArg("output", 2)),
     outputs=("output",),
     launch=_launch_matmul,
 )
@@ -78,9 +79,9 @@ def _launch_addmm(v, stream):
 addmm_kernel = Kernel(
     name="addmm",
     args=(
-        TensorArg("input", 2, HALF_DTYPES),
-        TensorArg("mat1", 2, HALF_DTYPES),
-        TensorArg("mat2", 2, HALF_DTYPES),
+        TensorArg("input", 2, GEMM_DTYPES),
+        TensorArg("mat1", 2, GEMM_DTYPES),
+        TensorArg("mat2", 2, GEMM_DTYPES),
         ScalarArg("beta"),
         ScalarArg("alpha"),
         TensorArg("output", 2),
@@ -116,11 +117,11 @@ def _launch_attention(v, stream):
 attention_kernel = Kernel(
     name="attention",
     args=(
-        TensorArg("q", 4, HALF_DTYPES),
-        TensorArg("k", 4, HALF_DTYPES),
-        TensorArg("v", 4, HALF_DTYPES),
+        TensorArg("q", 4, FLOAT_DTYPES),
+        TensorArg("k", 4, FLOAT_DTYPES),
+        TensorArg("v", 4, FLOAT_DTYPES),
         ScalarArg("is_causal"),
-        TensorArg("o", 4, HALF_DTYPES),
+        TensorArg("o", 4, FLOAT_DTYPES),
     ),
     outputs=("o",),
     launch=_launch_attention,

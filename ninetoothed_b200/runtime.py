@@ -34,6 +34,8 @@ class KernelLaunchError(RuntimeError):
 
 FLOAT_DTYPES = (torch.float16, torch.bfloat16, torch.float32)
 HALF_DTYPES = (torch.float16, torch.bfloat16)
+FP8_DTYPES = tuple(getattr(torch, name) for name in ("float8_e4m3fn", "float8_e5m2") if hasattr(torch, name))
+GEMM_DTYPES = HALF_DTYPES + FP8_DTYPES + (torch.float32,)
 
 
 def dtype_code(dtype: torch.dtype) -> int:

@@ -26,7 +26,7 @@ SOURCE = ORACLE_DIR / "oracle.c"
 BUILD_DIR = ORACLE_DIR / "_build"
 LIBRARY = BUILD_DIR / "liboracle.so"
 
-DTYPE_CODES = {"float16": 8, "bfloat16": 9, "float32": 10}
+DTYPE_CODES = {"float16": 8, "bfloat16": 9, "float32": 10, "float8_e4m3fn": 12, "float8_e5m2": 13}
 
 _lib = None
 

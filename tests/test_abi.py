@@ -64,7 +64,7 @@ def test_negative_sizes_rejected_without_launch(call):
 def test_unsupported_dtype_rejected_without_launch():
     lib = _lib.library()
     assert lib.nt_b200_softmax(None, None, 4, 4, 4, 1, 4, 1, 3, None) == 10002  # int64
-    assert lib.nt_b200_matmul(None, None, None, 1, 1, 1, 1, 1, 1, 1, 1, 1, 10, 8, None) == 10002  # fp32 in
+    assert lib.nt_b200_matmul(None, None, None, 1, 1, 1, 1, 1, 1, 1, 1, 1, 3, 8, None) == 10002  # int64 in
 
 
 def test_empty_launches_are_no_ops():

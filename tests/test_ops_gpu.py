@@ -206,6 +206,27 @@ def test_matmul_against_oracle(dtype, mnk):
     assert_within_steps(_np(out), oracle.matmul(a, b, "float16"), torch.float16, abs_sum=bound)
 
 
+@pytest.mark.parametrize("dtype", [getattr(torch, n) for n in ("float8_e4m3fn", "float8_e5m2") if hasattr(torch, n)])
+@pytest.mark.parametrize("mnk, rhs_transposed", (((512, 512, 512), True), ((384, 640, 256), False), ((200, 96, 48), True)))
+def test_matmul_fp8_against_oracle(dtype, mnk, rhs_transposed):
+    # tests/test_matmul.py:64-90 runs float8_e5m2 with a transposed rhs
+    m, n, k = mnk
+    a = torch.randn((m, k)).to(dtype)
+    b = (torch.randn((n, k)).to(dtype).t()) if rhs_transposed else torch.randn((k, n)).to(dtype)
+    out = programs.matmul(a.to(DEV), b.to(DEV))
+    bound = oracle.matmul(a.float().abs(), b.float().abs(), "float32")
+    assert_within_steps(_np(out), oracle.matmul(a, b, "float16"), torch.float16, abs_sum=bound)
+
+
+def test_addmm_fp8_against_oracle():
+    dtype = torch.float8_e5m2
+    inp, a = torch.randn(256, 320).to(dtype), torch.randn(256, 192).to(dtype)
+    b = torch.randn(320, 192).to(dtype).t()
+    out = programs.addmm(inp.to(DEV), a.to(DEV), b.to(DEV), beta=0.7, alpha=0.3)
+    ref = oracle.addmm(inp, a, b, 0.7, 0.3, "float16")
+    assert_within_steps(_np(out), ref, torch.float16, abs_sum=addmm_abs_sum(a.float(), b.float(), 0.3))
+
+
 def test_matmul_reference_case_vs_torch():
     # tests/test_matmul.py:69-90 (fp16 512^3); fp32-accumulated results agree
     # with torch.matmul to float16 rounding.
@@ -234,6 +255,18 @@ def test_matmul_output_dtypes(out_dtype):
     bound = oracle.matmul(a.abs(), b.abs(), "float32")
     steps_dtype = torch.bfloat16 if out_dtype == torch.bfloat16 else torch.float16
     assert_within_steps(_np(out), ref, steps_dtype, abs_sum=bound)
+
+
+def test_matmul_fp32_golden_and_baseline_cpu_config():
+    # fp32 512^3, N(0,1); the fixture is the reference kernel's output at 128^3.
+    g = golden_io.load("matmul_f32_128x128x128")
+    out = programs.matmul(golden_io.tensor(g["lhs"], DEV), golden_io.tensor(g["rhs"], DEV))
+    bound = oracle.matmul(np.abs(g["lhs"]), np.abs(g["rhs"]), "float32")
+    assert_within_steps(_np(out), g["output"].astype(np.float32), torch.float16, abs_sum=bound)
+    a, b = torch.randn(512, 512), torch.randn(512, 512)
+    out = programs.matmul(a.to(DEV), b.to(DEV))
+    bound = oracle.matmul(a.abs(), b.abs(), "float32")
+    assert_within_steps(_np(out), oracle.matmul(a, b, "float16"), torch.float16, abs_sum=bound)
 
 
 @pytest.mark.parametrize("name", golden_io.names("matmul_f16"))

@@ -107,3 +107,15 @@ def test_uniform_mapping_edges():
 def test_golden_fixtures_present():
     for prefix in ("matmul_", "addmm_", "attention_", "conv2d_", "max_pool2d_", "softmax_", "add_", "pow_", "dropout_"):
         assert golden_io.names(prefix), prefix
+
+
+@pytest.mark.parametrize("name", ["float8_e4m3fn", "float8_e5m2"])
+def test_fp8_rounding_matches_torch(name):
+    import torch
+
+    dtype = getattr(torch, name)
+    top = 440.0 if name == "float8_e4m3fn" else 50000.0
+    x = torch.cat([torch.randn(20000) * s for s in (1e-3, 0.1, 1.0, 30.0)] + [torch.linspace(-top, top, 4001)])
+    ref = x.to(dtype).float().numpy()
+    got = np.array([oracle.round_to(name, float(v)) for v in x.numpy()], dtype=np.float32)
+    np.testing.assert_array_equal(got, ref)

@@ -163,9 +163,11 @@ def test_make_runs_reference_program_on_b200(nt, name):
 # The reference's own operator tests (tests/test_*.py of the reference), run
 # unchanged with NINETOOTHED_BACKEND=cuda NINETOOTHED_PLATFORM=nvidia-b200, so
 # every `ninetoothed.make` / `@ninetoothed.jit` inside them builds on the B200
-# backend.  Parameters are the reference tests' own (float8 cases excluded: the
-# B200 contraction kernels take float16/bfloat16).
+# backend.  Parameters are the reference tests' own parametrisations.
 REFERENCE_CASES = [
+    ("test_matmul", dict(m=512, n=512, k=512, dtype=torch.float16, atol=1e-8)),
+    ("test_matmul", dict(m=512, n=512, k=512, dtype=torch.float8_e5m2, atol=0.125)),
+    ("test_addmm", dict(m=512, n=512, k=512, dtype=torch.float8_e5m2, atol=0.125)),
     ("test_add", dict(size=98432, dtype=torch.float32)),
     ("test_pow", dict(size=44925, dtype=torch.float32)),
     ("test_dropout", dict(size=349, dtype=torch.float16)),
@@ -179,6 +181,10 @@ REFERENCE_CASES = [
                             rtol=0.01, atol=0.01)),
     ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1, emb_dim=64, dtype=torch.float16, is_causal=True,
                             rtol=0.01, atol=0.01)),
+    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1024, emb_dim=64, dtype=torch.float32, is_causal=True,
+                            rtol=0.025, atol=0.025)),
+    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1, emb_dim=64, dtype=torch.float32, is_causal=False,
+                            rtol=0.025, atol=0.025)),
     ("test_conv2d", dict(n=4, c=64, h=16, w=16, k=512, r=3, s=3, padding=(1, 1), dtype=torch.float16, rtol=0.001,
                          atol=0.001)),
     ("test_conv2d", dict(n=4, c=64, h=16, w=16, k=512, r=3, s=3, padding=(2, 0), dtype=torch.float16, rtol=0.001,
