@@ -166,7 +166,12 @@ def _make_backend_class():
             auxiliary = shared_emitter._auxiliary_pointer_bindings(kernel.tensors)
             variables = public + tuple(binding["name"] for binding in auxiliary)
             shape_params = shared_emitter._shape_params(kernel.tensors, block.operations)
-            descriptor = {"program": program, "entrypoint": f"nt_b200_{program}", "library": "libnt_b200.so"}
+            # The artifact's entrypoint names the program, not a C symbol: a
+            # process without this plugin that reloads the artifact with the
+            # stock CUDA materializer then fails to find it, instead of binding
+            # the reference launcher's argument list to a libnt_b200 function.
+            descriptor = {"program": program, "entrypoint": f"b200.{program}", "c_symbol": f"nt_b200_{program}",
+                          "library": "libnt_b200.so"}
             metadata = {
                 "backend": Target.CUDA.value,
                 "target": dict(kernel.metadata.get("target", {})),
@@ -264,22 +269,31 @@ def _make_materializer_class():
         def __init__(self, fallback):
             self._fallback = fallback
 
-        def _materialize(self, compilation):
-            from ninetoothed.compiler.cache import compilation_cache_key, write_source
+        def _materialize(self, compilation, output_dir=None):
+            import dataclasses
+            from pathlib import Path
+
+            from ninetoothed.compiler.cache import atomic_write_text, compilation_cache_key, write_source
             from ninetoothed.compiler.runtime import Handle
 
             from ninetoothed_b200 import _lib
 
             program = compilation.artifact.metadata["b200_program"]
             _lib.library()  # fail loudly here if the library is missing
-            source = write_source(
-                compilation.artifact.kernel_name,
-                compilation.artifact.primary_source,
-                "b200.json",
-                cache_key=compilation_cache_key(compilation),
-            )
+            name, text = compilation.artifact.kernel_name, compilation.artifact.primary_source
+            if output_dir is None:
+                source = write_source(name, text, "b200.json", cache_key=compilation_cache_key(compilation))
+            else:
+                source = Path(output_dir) / f"{name}.b200.json"
+                atomic_write_text(source, text)
             launch = _bind(compilation.launch_abi, program, compilation.request.specialization_values)
-            return Handle(compilation, launch, launch, source, _lib.LIBRARY_PATH)
+            # The handle's manifest goes beside the descriptor (the cache or the
+            # AOT output directory), never beside the shared library inside the
+            # package; the built artifact still names the library it binds.
+            handle = Handle(compilation, launch, launch, source)
+            handle._library = str(_lib.LIBRARY_PATH)
+            handle._built_artifact = dataclasses.replace(handle._built_artifact, binary_path=str(_lib.LIBRARY_PATH))
+            return handle
 
         def jit_materialize(self, compilation, *, output_dir=None):
             if not _is_b200(compilation.artifact.metadata.get("target")):
@@ -289,7 +303,7 @@ def _make_materializer_class():
         def aot_build(self, compilation, *, output_dir):
             if not _is_b200(compilation.artifact.metadata.get("target")):
                 return self._fallback.aot_build(compilation, output_dir=output_dir)
-            return self._materialize(compilation)
+            return self._materialize(compilation, output_dir)
 
         def load_built_artifact(self, built):
             if not _is_b200(built.source.metadata.get("target")):

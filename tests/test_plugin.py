@@ -78,7 +78,8 @@ def test_reference_programs_are_recognised(nt, name):
     arrangement, application, tensors = _programs(nt)[name]
     compilation = _compile(nt, arrangement, application, tensors)
     assert compilation.artifact.metadata["b200_program"] == name
-    assert compilation.artifact.entrypoint == f"nt_b200_{name}"
+    # not a C symbol: the stock CUDA materializer must not bind it
+    assert compilation.artifact.entrypoint == f"b200.{name}"
 
 
 def test_unknown_program_is_rejected(nt):
@@ -103,6 +104,62 @@ def test_make_returns_handle_bound_to_b200_kernels(nt):
     # CPU tensors reach the B200 kernel's own device contract
     with pytest.raises(TypeError, match="CUDA device"):
         handle(a, a, a)
+
+
+def _aot_add_handle(nt, tmp_path):
+    from ninetoothed import Tensor
+    from ninetoothed.compiler import DEFAULT_COMPILER, CompileRequest
+
+    def arrangement(input, other, output):
+        return tuple(tensor.tile((64,)) for tensor in (input, other, output))
+
+    def application(input, other, output):
+        output = input + other  # noqa: F841
+
+    tensors = tuple(Tensor(shape=(257,), dtype=nt.float32) for _ in range(3))
+    compilation = DEFAULT_COMPILER.compile(
+        CompileRequest(arrangement=arrangement, application=application, tensors=tensors, backend="cuda",
+                       platform="nvidia-b200", kernel_name="reload_b200")
+    )
+    return DEFAULT_COMPILER.materialize(compilation, output_dir=tmp_path, mode="aot")
+
+
+def test_aot_build_records_a_reloadable_artifact(nt, tmp_path):
+    # mirrors the reference's tests/test_built_artifact_reload.py (AOT mode,
+    # BuiltArtifact with the library path and ABI manifest)
+    import pickle
+
+    from ninetoothed.compiler import load_built_artifact
+
+    import pathlib
+
+    package = pathlib.Path(__file__).resolve().parents[1] / "ninetoothed_b200"
+    handle = _aot_add_handle(nt, tmp_path)
+    built = handle._built_artifact
+    assert built.binary_path.endswith("libnt_b200.so")
+    assert pathlib.Path(built.source_path).parent == tmp_path
+    assert pathlib.Path(built.manifest_path).parent == tmp_path
+    assert not list(package.glob("*.manifest.json"))
+    assert built.source.metadata["b200_program"] == "add"
+    reloaded = load_built_artifact(pickle.loads(pickle.dumps(built)))
+    cpu = torch.empty(257)
+    with pytest.raises(TypeError, match="CUDA device"):
+        reloaded(cpu, cpu, cpu)
+
+
+@pytest.mark.gpu
+def test_aot_handle_and_reloaded_artifact_run_on_b200(nt, tmp_path):
+    from ninetoothed.compiler import load_built_artifact
+
+    handle = _aot_add_handle(nt, tmp_path)
+    x, y = torch.randn(257, device="cuda"), torch.randn(257, device="cuda")
+    out = torch.empty_like(x)
+    handle(x, y, out)
+    assert torch.equal(out, x + y)
+    reloaded = load_built_artifact(handle._built_artifact)
+    out2 = torch.empty_like(x)
+    reloaded(x, y, out2)
+    assert torch.equal(out2, x + y)
 
 
 def test_other_platforms_keep_the_stock_cuda_backend(nt):
