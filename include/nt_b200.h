@@ -194,11 +194,14 @@ int nt_b200_conv2d(const void *input, const void *filter, void *output, int64_t 
 
 /*
  * Workspace bytes the tensor-core conv2d path needs for this problem (0 when
- * the path does not apply: 32-bit dtype or channels not a multiple of 8).
- * No counterpart in the reference (its conv2d program stages nothing).
+ * the path does not apply: 32-bit dtype or channels not a multiple of 8): the
+ * input as NHWC with pad_w zero columns on each side of every row, then the
+ * filter as KRSC.  No counterpart in the reference (its conv2d program stages
+ * nothing).
  */
 int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w,
-                                      int64_t k, int64_t r, int64_t s, int dtype);
+                                      int64_t k, int64_t r, int64_t s, int64_t pad_h,
+                                      int64_t pad_w, int dtype);
 
 /*
  * conv2d exactly as nt_b200_conv2d, for callers that cannot provide device

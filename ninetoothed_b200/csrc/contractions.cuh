@@ -137,10 +137,10 @@ extern "C" int nt_b200_conv2d(const void *input, const void *filter, void *outpu
 }
 
 extern "C" int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k, int64_t r,
-                                                 int64_t s, int dtype) {
-  if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0) return 0;
+                                                 int64_t s, int64_t pad_h, int64_t pad_w, int dtype) {
+  if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0 || pad_h < 0 || pad_w < 0) return 0;
   if (!nt::is_half_dtype(dtype)) return 0;
-  return nt::tc::conv_workspace_bytes(n, c, h, w, k, r, s, 2);
+  return nt::tc::conv_workspace_bytes(n, c, h, w, k, r, s, pad_w, 2);
 }
 
 extern "C" int nt_b200_attention(const void *q, const void *k, const void *v, int is_causal, void *o,

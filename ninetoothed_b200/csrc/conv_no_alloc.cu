@@ -1,7 +1,7 @@
 // nt_b200_conv2d_no_alloc: conv2d for callers that cannot hand the library a
 // workspace.
 //
-// nt_b200_conv2d stages the input (NHWC) and the filter (KRSC) in device memory
+// nt_b200_conv2d stages the input (W-padded NHWC) and the filter (KRSC) in device memory
 // the caller passes in.  Some callers have no way to provide it at call time: a
 // plain C host program that owns no device allocator, a serving loop that must
 // not call cudaMalloc because it synchronises the whole device and stalls every
@@ -68,7 +68,7 @@ extern "C" int nt_b200_conv2d_no_alloc(const void *input, const void *filter, vo
                                        int64_t h, int64_t w, int64_t k, int64_t r, int64_t s, int64_t pad_h,
                                        int64_t pad_w, const int64_t *input_strides, const int64_t *filter_strides,
                                        const int64_t *output_strides, int dtype, void *stream) {
-  const int64_t need = nt_b200_conv2d_workspace_size(n, c, h, w, k, r, s, dtype);
+  const int64_t need = nt_b200_conv2d_workspace_size(n, c, h, w, k, r, s, pad_h, pad_w, dtype);
   if (need > nt::no_alloc::kConvStaticWorkspaceBytes) return NT_B200_ERR_WORKSPACE_TOO_LARGE;
   void *scratch = nullptr;
   if (need > 0 && n * k * (h + 2 * pad_h - r + 1) * (w + 2 * pad_w - s + 1) > 0) {

@@ -101,10 +101,11 @@ struct Params {
   int64_t sim, sin;
   float beta, alpha;  // rounded to TI and float16 (addmm_value)
   int tiles_m, tiles_n, num_kb;
-  // conv2d implicit GEMM (EPI == kConv): output tile = BP x BQ output pixels of
-  // one image; k-block kb = (r, s, channel block cb).
-  int conv_c_blocks, conv_s, conv_pad_h, conv_pad_w;
-  int conv_bp, conv_bq, conv_p_blocks, conv_q_blocks, conv_P, conv_Q;
+  // conv2d implicit GEMM (EPI == kConv): an m-block is 128 consecutive
+  // positions pos = p * Wp + q of one image on the W-padded grid (Wp = W +
+  // 2 pad_w columns; positions with q >= Q are computed and dropped); k-block
+  // kb = (r, s, channel block cb).
+  int conv_c_blocks, conv_s, conv_pad_h, conv_wp, conv_tiles_img, conv_P, conv_Q;
   int64_t conv_osn, conv_osk, conv_osp, conv_osq;
 };
 
@@ -139,16 +140,6 @@ __device__ __forceinline__ void store_row_chunk(TO *dst, const float (&v)[32], b
     for (int e = 0; e < 32; ++e)
       if (e < valid) dst[e] = from_f<TO>(v[e]);
   }
-}
-
-// Output-tile origin of a conv2d m-block: image, first output row, first column.
-__device__ __forceinline__ void conv_tile(const Params &prm, int mb, int &img, int &p0, int &q0) {
-  const int qb = mb % prm.conv_q_blocks;
-  const int t = mb / prm.conv_q_blocks;
-  const int pb = t % prm.conv_p_blocks;
-  img = t / prm.conv_p_blocks;
-  p0 = pb * prm.conv_bp;
-  q0 = qb * prm.conv_bq;
 }
 
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
@@ -213,15 +204,17 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           ptx::mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
           const int k0 = kb * kblock<TI>();
           if constexpr (EPI == Epilogue::kConv) {
-            // A: BP x BQ pixels x 64 channels of the NHWC input at filter tap
-            // (r, s); coordinates outside the image read as zero (the padding).
+            // A: 128 consecutive rows x 64 channels of the W-padded NHWC input
+            // of one image, shifted by filter tap (r, s): position pos reads
+            // row pos + (r - pad_h) * Wp + s.  Rows above or below the image
+            // (negative or >= H * Wp) read as zero, which is the H padding;
+            // the W padding is stored as zero columns.
             // B: 256 output channels x 64 input channels of the KRSC filter.
             const int cb = kb % prm.conv_c_blocks, rs = kb / prm.conv_c_blocks;
             const int r = rs / prm.conv_s, sx = rs % prm.conv_s;
-            int img, p0, q0;
-            conv_tile(prm, mb, img, p0, q0);
-            ptx::tma_load_4d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, cb * BK, q0 + sx - prm.conv_pad_w,
-                             p0 + r - prm.conv_pad_h, img);
+            const int img = mb / prm.conv_tiles_img, pos0 = (mb % prm.conv_tiles_img) * BM;
+            ptx::tma_load_3d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, cb * BK,
+                             pos0 + (r - prm.conv_pad_h) * prm.conv_wp + sx, img);
             ptx::tma_load_3d(b_base + stage * B_STAGE_BYTES, &tmap_b, fb, cb * BK, rs, n0);
           } else {
           ptx::tma_load_2d(a_base + stage * A_STAGE_BYTES, &tmap_a, fb, k0, m0);
@@ -294,10 +287,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       const bool row_ok = m < prm.M;
       TO *out = static_cast<TO *>(prm.out);
       if constexpr (EPI == Epilogue::kConv) {
-        // TMEM lane = pixel (hp, wq) of the tile; columns = output channels.
-        int img, p0, q0;
-        conv_tile(prm, mb, img, p0, q0);
-        const int p = p0 + row_in_tile / prm.conv_bq, q = q0 + row_in_tile % prm.conv_bq;
+        // TMEM lane = position p * Wp + q of the tile; columns = output channels.
+        const int img = mb / prm.conv_tiles_img, pos = (mb % prm.conv_tiles_img) * BM + row_in_tile;
+        const int p = pos / prm.conv_wp, q = pos % prm.conv_wp;
         const bool pix_ok = p < prm.conv_P && q < prm.conv_Q;
         TO *pix = out + (int64_t)img * prm.conv_osn + (int64_t)p * prm.conv_osp + (int64_t)q * prm.conv_osq;
 #pragma unroll 1
@@ -412,15 +404,67 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
 }
 
 // ------------------------------------------------------------------ conv2d staging
-// NCHW (any strides) -> dense NHWC, one 64-channel x 64-pixel tile per CTA
+// The staged input is NHWC with pad_w zero columns on each side of every row
+// (row width Wp = W + 2 pad_w): pixel (h, w) of image n sits at row
+// (n * H + h) * Wp + w + pad_w of a [n * H * Wp, C] matrix.
+
+// Zeroes the pad_w columns on both sides of the staged rows whose first pixel
+// lies in this CTA's pixel range [p0, p0 + 64), for channels [c0, c0 + 64):
+// every row is zeroed by exactly one CTA per channel block.  C is a multiple
+// of 8, so 16-byte stores.
+template <typename T>
+__device__ __forceinline__ void zero_pad_columns(T *dst, int p0, int HW, int W, int wp, int pad_w, int c0, int C,
+                                                 int t) {
+  if (pad_w == 0) return;
+  const int end = p0 + 64 < HW ? p0 + 64 : HW;
+  const int h_first = (p0 + W - 1) / W, h_last = (end - 1) / W;
+  const int per_row = 2 * pad_w * 8;  // columns x 8 vectors of 8 channels
+  for (int j = t; j < (h_last - h_first + 1) * per_row; j += 256) {
+    const int h = h_first + j / per_row, rem = j % per_row, col = rem / 8, c = c0 + (rem % 8) * 8;
+    const int qp = col < pad_w ? col : W + col;  // right side: W + pad_w + (col - pad_w)
+    if (c < C) *reinterpret_cast<int4 *>(dst + ((int64_t)h * wp + qp) * C + c) = make_int4(0, 0, 0, 0);
+  }
+}
+
+// KCRS filter (any strides) -> dense KRSC.  Done by the first z-plane of the
+// input-staging grid (scheduled first), so it runs alongside the memory-bound
+// input transpose instead of as a launch of its own: CTA `block` of `blocks`
+// handles output channels k = block, block + blocks, ...
+template <typename T>
+struct FilterStaging {
+  const T *in;
+  T *out;
+  int K, C, R, S;
+  int64_t sk, sc, sr, ss;
+};
+
+template <typename T>
+__device__ __forceinline__ void stage_filter(const FilterStaging<T> &f, int block, int blocks) {
+  const int RS = f.R * f.S, total = RS * f.C;
+  for (int k = block; k < f.K; k += blocks) {
+    const T *src = f.in + (int64_t)k * f.sk;
+    T *dst = f.out + (int64_t)k * total;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+      const int rs = i / f.C, c = i % f.C;
+      dst[i] = src[(int64_t)c * f.sc + (int64_t)(rs / f.S) * f.sr + (int64_t)(rs % f.S) * f.ss];
+    }
+  }
+}
+
+// NCHW (any strides) -> W-padded NHWC, one 64-channel x 64-pixel tile per CTA
 // through shared memory, so both the reads (along pixels) and the writes
 // (along channels) are contiguous runs.
 template <typename T>
 __global__ void __launch_bounds__(256)
-nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int64_t isn, int64_t isc,
-                    int64_t ish, int64_t isw) {
+nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int wp, int pad_w,
+                    int64_t isn, int64_t isc, int64_t ish, int64_t isw, FilterStaging<T> filter) {
+  if (blockIdx.z == 0) {
+    stage_filter(filter, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    return;
+  }
   __shared__ T tile[64][64 + 2];
-  const int n = blockIdx.z, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
+  const int n = blockIdx.z - 1, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
   const int t = threadIdx.x;
   const T *src = in + (int64_t)n * isn;
 #pragma unroll
@@ -430,78 +474,75 @@ nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW
     if (c < C && pix < HW) tile[cc][pp] = src[(int64_t)c * isc + (int64_t)(pix / W) * ish + (int64_t)(pix % W) * isw];
   }
   __syncthreads();
-  T *dst = out + (int64_t)n * HW * C;
+  T *dst = out + (int64_t)n * (HW / W) * wp * C;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
     const int pp = t / 64 + 4 * i, cc = t % 64;
     const int c = c0 + cc, pix = p0 + pp;
-    if (c < C && pix < HW) dst[(int64_t)pix * C + c] = tile[cc][pp];
+    if (c < C && pix < HW) dst[((int64_t)(pix / W) * wp + pix % W + pad_w) * C + c] = tile[cc][pp];
   }
+  zero_pad_columns(dst, p0, HW, W, wp, pad_w, c0, C, t);
 }
 
-// Contiguous-plane NCHW -> NHWC (each (n, c) plane dense, HW a multiple of 8,
-// 16-byte aligned planes): a 64-channel x 64-pixel tile per CTA moves through
-// shared memory with 16-byte loads along pixels and 16-byte stores along
-// channels, no index division per element.
+// Contiguous-plane NCHW -> W-padded NHWC (each (n, c) plane dense, HW a
+// multiple of 8, 16-byte aligned planes, C a multiple of 8): a 64-channel x
+// 64-pixel tile per CTA.  Each thread loads 8 pixels of two adjacent channels
+// (16 bytes each), interleaves them into channel pairs and writes 8 words of a
+// [pixel][channel] tile in shared memory; then 8 lanes store each pixel's 64
+// channels as one contiguous 128-byte run.  The tile's 16-byte chunks are
+// XOR-swizzled by (pixel / 8) so that both passes are free of bank conflicts.
 template <typename T>
 __global__ void __launch_bounds__(256)
-nchw_to_nhwc_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int64_t isn, int64_t isc) {
+nchw_to_nhwc_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int wp, int pad_w,
+                        int64_t isn, int64_t isc, FilterStaging<T> filter) {
   static_assert(sizeof(T) == 2, "16-bit elements");
-  __shared__ __align__(16) T tile[64][64 + 8];  // [channel][pixel], rows padded by 16 bytes
-  const int n = blockIdx.z, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
+  if (blockIdx.z == 0) {
+    stage_filter(filter, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+    return;
+  }
+  __shared__ __align__(16) uint32_t tile[64][32];  // [pixel][channel pair]
+  const int n = blockIdx.z - 1, c0 = blockIdx.y * 64, p0 = blockIdx.x * 64;
   const int t = threadIdx.x;
-  const T *src = in + (int64_t)n * isn;
-  // load: 64 channels x 8 vectors of 8 pixels
+  {
+    const int cp = t / 8, pv = t % 8;  // channel pair 0..31, pixel group 0..7
+    const int c = c0 + 2 * cp, pix = p0 + pv * 8;
+    const T *src = in + (int64_t)n * isn + (int64_t)c * isc + pix;
+    int4 a = make_int4(0, 0, 0, 0), b = make_int4(0, 0, 0, 0);
+    if (pix < HW && c < C) {  // C % 8 == 0, so channel c + 1 exists too
+      a = __ldcs(reinterpret_cast<const int4 *>(src));
+      b = __ldcs(reinterpret_cast<const int4 *>(src + isc));
+    }
+    const uint32_t wa[4] = {(uint32_t)a.x, (uint32_t)a.y, (uint32_t)a.z, (uint32_t)a.w};
+    const uint32_t wb[4] = {(uint32_t)b.x, (uint32_t)b.y, (uint32_t)b.z, (uint32_t)b.w};
+    const int word = ((cp / 4) ^ pv) * 4 + cp % 4;  // rows pv * 8 + e all have row / 8 == pv
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int v = t + 256 * i;   // 0..511
-    const int cc = v / 8, pv = v % 8;
-    const int c = c0 + cc, pix = p0 + pv * 8;
-    int4 val = make_int4(0, 0, 0, 0);
-    if (c < C && pix < HW) val = __ldcs(reinterpret_cast<const int4 *>(src + (int64_t)c * isc + pix));
-    *reinterpret_cast<int4 *>(&tile[cc][pv * 8]) = val;
+    for (int j = 0; j < 4; ++j) {  // word j of a load holds pixels 2j (low half) and 2j + 1
+      tile[pv * 8 + 2 * j][word] = __byte_perm(wa[j], wb[j], 0x5410);
+      tile[pv * 8 + 2 * j + 1][word] = __byte_perm(wa[j], wb[j], 0x7632);
+    }
   }
   __syncthreads();
-  // store: 64 pixels x 8 vectors of 8 channels; a warp takes 32 consecutive
-  // pixels of one channel group, so its shared-memory reads are one
-  // contiguous 64-byte run per channel
-  T *dst = out + (int64_t)n * HW * C;
+  T *dst = out + (int64_t)n * (HW / W) * wp * C;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int v = t + 256 * i;
-    const int pp = v % 64, cv = v / 64;
+    const int pp = v / 8, cv = v % 8;  // pixel 0..63, vector of 8 channels 0..7
     const int pix = p0 + pp, c = c0 + cv * 8;
     if (pix < HW && c < C) {
-      alignas(16) T pk[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) pk[e] = tile[cv * 8 + e][pp];
-      *reinterpret_cast<int4 *>(dst + (int64_t)pix * C + c) = *reinterpret_cast<int4 *>(pk);
+      const int4 val = *reinterpret_cast<const int4 *>(&tile[pp][((cv ^ (pp / 8)) & 7) * 4]);
+      const int64_t row = (int64_t)(pix / W) * wp + pix % W + pad_w;
+      *reinterpret_cast<int4 *>(dst + row * C + c) = val;
     }
   }
+  zero_pad_columns(dst, p0, HW, W, wp, pad_w, c0, C, t);
 }
 
-// KCRS filter (any strides) -> dense KRSC.
-template <typename T>
-__global__ void kcrs_to_krsc_kernel(const T *__restrict__ in, T *__restrict__ out, int K, int C, int R, int S,
-                                    int64_t sk, int64_t sc, int64_t sr, int64_t ss) {
-  const int64_t total = (int64_t)K * R * S * C;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    int64_t t = i / C;
-    const int sx = (int)(t % S);
-    t /= S;
-    const int r = (int)(t % R);
-    const int k = (int)(t / R);
-    out[i] = in[k * sk + c * sc + r * sr + sx * ss];
-  }
-}
-
-// Workspace of the tensor-core conv2d path: dense NHWC input, then the KRSC
-// filter at the next 256-byte boundary.  0 when the path does not apply.
+// Workspace of the tensor-core conv2d path: the W-padded NHWC input, then the
+// KRSC filter at the next 256-byte boundary.  0 when the path does not apply.
 inline int64_t conv_workspace_bytes(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k, int64_t r, int64_t s,
-                                    int elem) {
+                                    int64_t pad_w, int elem) {
   if (elem != 2 || c % 8 != 0) return 0;
-  const int64_t act = n * h * w * c * elem;
+  const int64_t act = n * h * (w + 2 * pad_w) * c * elem;
   const int64_t flt = k * r * s * c * elem;
   return ((act + 255) / 256) * 256 + flt;
 }
@@ -512,35 +553,32 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     return kNotEligible;
   } else {
     using namespace gemm;
-    const int64_t need = conv_workspace_bytes(p.n, p.c, p.h, p.w, p.k, p.r, p.s, 2);
+    const int64_t need = conv_workspace_bytes(p.n, p.c, p.h, p.w, p.k, p.r, p.s, p.pad_w, 2);
     if (need == 0 || workspace == nullptr || workspace_bytes < need) return kNotEligible;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kNotEligible;
-    if (p.n > (1 << 16) || p.c > (1 << 20) || p.h > (1 << 20) || p.w > (1 << 20) || p.k > (1 << 20) ||
-        p.r * p.s > (1 << 20) || p.h * p.w > (1LL << 31) - 1)
+    const int64_t wp = p.w + 2 * p.pad_w;
+    if (p.h == 0 || p.w == 0 || p.n >= 65535 || p.c > (1 << 20) || p.h > (1 << 20) || wp > (1 << 20) ||
+        p.k > (1 << 20) || p.r * p.s * p.c > (1 << 30) || p.pad_h > (1 << 20) ||
+        (p.h + 2 * p.pad_h + p.r) * wp > (1LL << 30))
       return kNotEligible;
-    // Output tile: BP rows x BQ columns of one image, BQ the power of two >= Q
-    // (at most 128), BP * BQ = 128 pixels.
-    int bq = 1;
-    while (bq < p.Q && bq < 128) bq <<= 1;
-    if (bq < 8) bq = 8;  // 16 rows at most per tile
-    const int bp = BM / bq;
     T *act = static_cast<T *>(workspace);
-    T *flt = reinterpret_cast<T *>(static_cast<uint8_t *>(workspace) + ((p.n * p.h * p.w * p.c * 2 + 255) / 256) * 256);
+    T *flt = reinterpret_cast<T *>(static_cast<uint8_t *>(workspace) + ((p.n * p.h * wp * p.c * 2 + 255) / 256) * 256);
     {
       const int HW = (int)(p.h * p.w);
-      dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)p.n);
+      // z-plane 0: the filter; planes 1 .. n: the images
+      dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)(p.n + 1));
+      const FilterStaging<T> filter{static_cast<const T *>(p.filter), flt, (int)p.k, (int)p.c, (int)p.r, (int)p.s,
+                                    p.fs[0], p.fs[1], p.fs[2], p.fs[3]};
       const bool dense_planes = p.is[3] == 1 && p.is[2] == p.w && HW % 8 == 0 && p.is[1] % 8 == 0 &&
                                 p.is[0] % 8 == 0 && (reinterpret_cast<uintptr_t>(p.input) & 15u) == 0;
       if (dense_planes)
         nchw_to_nhwc_vec_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
-                                                             p.is[0], p.is[1]);
+                                                             (int)p.w, (int)wp, (int)p.pad_w, p.is[0], p.is[1],
+                                                             filter);
       else
         nchw_to_nhwc_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
-                                                         (int)p.w, p.is[0], p.is[1], p.is[2], p.is[3]);
-      const int64_t total = p.k * p.r * p.s * p.c;
-      const int blocks = (int)((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
-      kcrs_to_krsc_kernel<T><<<blocks, 256, 0, stream>>>(static_cast<const T *>(p.filter), flt, (int)p.k, (int)p.c,
-                                                         (int)p.r, (int)p.s, p.fs[0], p.fs[1], p.fs[2], p.fs[3]);
+                                                         (int)p.w, (int)wp, (int)p.pad_w, p.is[0], p.is[1],
+                                                         p.is[2], p.is[3], filter);
       const int st = launch_status();
       if (st != 0) return st;
     }
@@ -548,12 +586,13 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     if (!fn) return kNotEligible;
     CUtensorMap ta, tb;
     {
-      const cuuint64_t dims[4] = {(cuuint64_t)p.c, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
-      const cuuint64_t strides[3] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.w * p.c * 2),
-                                     (cuuint64_t)(p.h * p.w * p.c * 2)};
-      const cuuint32_t box[4] = {64, (cuuint32_t)bq, (cuuint32_t)bp, 1};
-      const cuuint32_t estr[4] = {1, 1, 1, 1};
-      if (fn(&ta, tmap_dtype<T>(), 4, act, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+      // [image][H * Wp rows][C]: one image per outer index, so rows shifted
+      // above or below an image read as zero instead of a neighbour's pixels
+      const cuuint64_t dims[3] = {(cuuint64_t)p.c, (cuuint64_t)(p.h * wp), (cuuint64_t)p.n};
+      const cuuint64_t strides[2] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.h * wp * p.c * 2)};
+      const cuuint32_t box[3] = {64, (cuuint32_t)BM, 1};
+      const cuuint32_t estr[3] = {1, 1, 1};
+      if (fn(&ta, tmap_dtype<T>(), 3, act, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return kNotEligible;
@@ -573,18 +612,15 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     prm.conv_c_blocks = (int)((p.c + BK - 1) / BK);
     prm.conv_s = (int)p.s;
     prm.conv_pad_h = (int)p.pad_h;
-    prm.conv_pad_w = (int)p.pad_w;
-    prm.conv_bp = bp;
-    prm.conv_bq = bq;
-    prm.conv_p_blocks = (int)((p.P + bp - 1) / bp);
-    prm.conv_q_blocks = (int)((p.Q + bq - 1) / bq);
+    prm.conv_wp = (int)wp;
+    prm.conv_tiles_img = (int)((p.P * wp + BM - 1) / BM);
     prm.conv_P = (int)p.P;
     prm.conv_Q = (int)p.Q;
     prm.conv_osn = p.os[0];
     prm.conv_osk = p.os[1];
     prm.conv_osp = p.os[2];
     prm.conv_osq = p.os[3];
-    const int64_t tiles_m = p.n * prm.conv_p_blocks * prm.conv_q_blocks;
+    const int64_t tiles_m = p.n * prm.conv_tiles_img;
     prm.tiles_m = (int)tiles_m;
     prm.tiles_n = (int)((p.k + BN - 1) / BN);
     prm.num_kb = (int)(p.r * p.s * prm.conv_c_blocks);

@@ -148,7 +148,7 @@ def _launch_conv2d(v, stream):
     code = dtype_code(x.dtype)
     # Workspace for the NHWC / KRSC staging of the tensor-core path, from the
     # caching allocator on the launch stream (the C ABI never allocates).
-    nbytes = _lib_call("nt_b200_conv2d_workspace_size", n, c, h, wd, k, r, s, code)
+    nbytes = _lib_call("nt_b200_conv2d_workspace_size", n, c, h, wd, k, r, s, ph, pw, code)
     workspace = torch.empty(max(nbytes, 0), dtype=torch.uint8, device=x.device) if nbytes > 0 else None
     return _lib_call(
         "nt_b200_conv2d", ptr(x), ptr(w), ptr(out), n, c, h, wd, k, r, s, ph, pw, xs, ws, os_,

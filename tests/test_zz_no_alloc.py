@@ -39,7 +39,7 @@ def _with_workspace(lib, x, w, padding, dtype_code, stream):
     n, c, h, wd = x.shape
     k, _, r, s = w.shape
     out = torch.empty(n, k, h + 2 * padding[0] - r + 1, wd + 2 * padding[1] - s + 1, device=x.device, dtype=x.dtype)
-    nbytes = lib.nt_b200_conv2d_workspace_size(n, c, h, wd, k, r, s, dtype_code)
+    nbytes = lib.nt_b200_conv2d_workspace_size(n, c, h, wd, k, r, s, padding[0], padding[1], dtype_code)
     workspace = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
     rc = lib.nt_b200_conv2d(*_conv_args(x, w, out, padding), ctypes.c_void_p(workspace.data_ptr()), nbytes,
                             dtype_code, stream)
@@ -81,8 +81,8 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
 
 def test_no_alloc_rejects_problems_beyond_the_fixed_array():
     lib = _lib.library()
-    # NHWC staging of 64 x 256 x 56 x 56 float16 is about 98 MiB > 64 MiB
-    need = lib.nt_b200_conv2d_workspace_size(64, 256, 56, 56, 256, 3, 3, FLOAT16)
+    # NHWC staging of 64 x 256 x 56 x (56 + 2) float16 is about 102 MiB > 64 MiB
+    need = lib.nt_b200_conv2d_workspace_size(64, 256, 56, 56, 256, 3, 3, 1, 1, FLOAT16)
     assert need > STATIC_BYTES
     strides = _lib.int64_array((1, 1, 1, 1))
     rc = lib.nt_b200_conv2d_no_alloc(None, None, None, 64, 256, 56, 56, 256, 3, 3, 1, 1, strides, strides, strides,
