@@ -142,6 +142,76 @@ __device__ __forceinline__ void store_row_chunk(TO *dst, const float (&v)[32], b
   }
 }
 
+// Epilogue of one accumulator: this warp's 32 TMEM lanes (tile rows
+// quarter * 32 + lane) x 256 columns starting at TMEM column `col0`.  Row r of
+// the tile is output row row0 + r (matmul, addmm), or position row0 + r
+// (= p * Wp + q) of image `img` (conv2d); columns are outputs n0, n0 + 1, ...
+template <typename TI, typename TO, Epilogue EPI>
+__device__ __forceinline__ void store_accumulator(const Params &prm, uint32_t tmem_base, uint32_t col0, int quarter,
+                                                  int lane, int64_t row0, int64_t n0, int img) {
+  const int row_in_tile = quarter * 32 + lane;
+  const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + col0;
+  TO *out = static_cast<TO *>(prm.out);
+  if constexpr (EPI == Epilogue::kConv) {
+    // TMEM lane = position p * Wp + q; columns = output channels.
+    const int pos = (int)row0 + row_in_tile;
+    const int p = pos / prm.conv_wp, q = pos % prm.conv_wp;
+    const bool pix_ok = p < prm.conv_P && q < prm.conv_Q;
+    TO *pix = out + (int64_t)img * prm.conv_osn + (int64_t)p * prm.conv_osp + (int64_t)q * prm.conv_osq;
+#pragma unroll 1
+    for (int c = 0; c < 256 / 32; ++c) {
+      uint32_t raw[32];
+      ptx::tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), raw);
+      ptx::tmem_ld_wait();
+      const int64_t nc = n0 + c * 32;
+      if (!pix_ok || nc >= prm.N) continue;
+      const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
+      TO *dst = pix + nc * prm.conv_osk;
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        if (e < valid) dst[e * prm.conv_osk] = from_f<TO>(round_f16(__uint_as_float(raw[e])));
+    }
+  } else {
+    const int64_t m = row0 + row_in_tile;
+    const bool row_ok = m < prm.M;
+#pragma unroll 1
+    for (int c = 0; c < 256 / 32; ++c) {
+      uint32_t raw[32];
+      ptx::tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), raw);
+      ptx::tmem_ld_wait();
+      const int64_t nc = n0 + c * 32;
+      if (!row_ok || nc >= prm.N) continue;
+      const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
+      float v[32];
+      if constexpr (EPI == Epilogue::kMatmul) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
+      } else if constexpr (EPI == Epilogue::kAddmm) {
+        const TI *bias = static_cast<const TI *>(prm.bias) + m * prm.sim + nc * prm.sin;
+        alignas(16) TI in_v[32];
+        if (valid == 32 && prm.sin == 1 && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0) {
+          // the row's 32 inputs are one contiguous run: 16-byte loads
+#pragma unroll
+          for (int i = 0; i < 32 * (int)sizeof(TI) / 16; ++i)
+            reinterpret_cast<int4 *>(in_v)[i] = __ldcs(reinterpret_cast<const int4 *>(bias) + i);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) in_v[e] = e < valid ? bias[e * prm.sin] : from_f<TI>(0.f);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = addmm_value<TI>(prm.beta, prm.alpha, to_f(in_v[e]), __uint_as_float(raw[e]));
+      }
+      TO *dst = out + m * prm.som + nc * prm.son;
+      const bool vec = valid == 32 && prm.son == 1 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
+      if (vec || prm.son == 1) {
+        store_row_chunk<TO>(dst, v, vec, valid);
+      } else {
+        for (int e = 0; e < valid; ++e) dst[e * prm.son] = from_f<TO>(v[e]);
+      }
+    }
+  }
+}
+
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, Params prm) {
@@ -273,7 +343,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
   } else {
     // ---------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    const int row_in_tile = quarter * 32 + lane;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -282,60 +351,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       ptx::tc_fence_after();
       int mb, nb;
       tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
-      const int64_t m = (int64_t)mb * BM + row_in_tile;
-      const int64_t n0 = (int64_t)nb * BN;
-      const bool row_ok = m < prm.M;
-      TO *out = static_cast<TO *>(prm.out);
-      if constexpr (EPI == Epilogue::kConv) {
-        // TMEM lane = position p * Wp + q of the tile; columns = output channels.
-        const int img = mb / prm.conv_tiles_img, pos = (mb % prm.conv_tiles_img) * BM + row_in_tile;
-        const int p = pos / prm.conv_wp, q = pos % prm.conv_wp;
-        const bool pix_ok = p < prm.conv_P && q < prm.conv_Q;
-        TO *pix = out + (int64_t)img * prm.conv_osn + (int64_t)p * prm.conv_osp + (int64_t)q * prm.conv_osq;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t raw[32];
-          ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32),
-                                  raw);
-          ptx::tmem_ld_wait();
-          const int64_t nc = n0 + c * 32;
-          if (!pix_ok || nc >= prm.N) continue;
-          const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
-          TO *dst = pix + nc * prm.conv_osk;
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (e < valid) dst[e * prm.conv_osk] = from_f<TO>(round_f16(__uint_as_float(raw[e])));
-        }
-      } else {
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t raw[32];
-        ptx::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * BN + c * 32), raw);
-        ptx::tmem_ld_wait();
-        const int64_t nc = n0 + c * 32;
-        if (!row_ok || nc >= prm.N) continue;
-        const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
-        float v[32];
-        if constexpr (EPI == Epilogue::kMatmul) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
-        } else if constexpr (EPI == Epilogue::kAddmm) {
-          const TI *bias = static_cast<const TI *>(prm.bias) + m * prm.sim + nc * prm.sin;
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float in = e < valid ? to_f(bias[e * prm.sin]) : 0.f;
-            v[e] = addmm_value<TI>(prm.beta, prm.alpha, in, __uint_as_float(raw[e]));
-          }
-        }
-        TO *dst = out + m * prm.som + nc * prm.son;
-        const bool vec = valid == 32 && prm.son == 1 && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0);
-        if (vec || prm.son == 1) {
-          store_row_chunk<TO>(dst, v, vec, valid);
-        } else {
-          for (int e = 0; e < valid; ++e) dst[e * prm.son] = from_f<TO>(v[e]);
-        }
-      }
-      }
+      if constexpr (EPI == Epilogue::kConv)
+        store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
+                                       (int64_t)(mb % prm.conv_tiles_img) * BM, (int64_t)nb * BN,
+                                       mb / prm.conv_tiles_img);
+      else
+        store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane, (int64_t)mb * BM,
+                                       (int64_t)nb * BN, 0);
       ptx::tc_fence_before();
       ptx::mbar_arrive(tempty_bar(buf));
     }
@@ -350,6 +372,237 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
 }
 
 }  // namespace gemm
+
+// ------------------------------------------------------------------ CTA-pair kernel
+// The same GEMM on CTA pairs (thread-block clusters of 2) with tcgen05
+// .cta_group::2: a pair computes a 256 x 256 output tile with M = 256 MMAs
+// issued by the even CTA.  Each CTA stages its own 128 rows of A and its half
+// (128 columns) of B, so every operand byte crosses from L2 once per pair tile
+// instead of B being fetched by two independent 128-row tiles: 32 KB per CTA
+// per 64-element k-block instead of 48 KB, which lets six stages fit in
+// shared memory.  Both CTAs' loads complete on the even CTA's `full` barrier;
+// the MMA commits release the stage (and publish the accumulator) in both
+// CTAs; both CTAs' epilogue warps release the accumulator on the even CTA's
+// `tempty` barrier.
+namespace gemm2 {
+
+constexpr int BM = 128;      // A rows per CTA; the pair tile is 2 * BM = 256 rows
+constexpr int BN = 256;      // output columns of a pair tile
+constexpr int BN_CTA = 128;  // B rows (output columns) staged per CTA
+constexpr int STAGES = 7;
+constexpr int A_STAGE_BYTES = BM * 128;      // 16 KB
+constexpr int B_STAGE_BYTES = BN_CTA * 128;  // 16 KB
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+
+using gemm::Params;
+using gemm::kblock;
+using gemm::mma_k;
+
+template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                 Params prm) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = ptx::smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;  // same offset in both CTAs
+  uint8_t *smem = smem_raw + (base - raw_addr);
+  const uint32_t a_base = base;
+  const uint32_t b_base = base + STAGES * A_STAGE_BYTES;
+  uint8_t *ctrl = smem + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES);
+  const uint32_t ctrl_addr = ptx::smem_u32(ctrl);
+  // barriers: full[S] (used on the even CTA), empty[S], tfull[2], tempty[2]
+  // (used on the even CTA); then the TMEM base and the abort flag
+  auto full_bar = [&](int s) { return ctrl_addr + 8u * s; };
+  auto empty_bar = [&](int s) { return ctrl_addr + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int b) { return ctrl_addr + 8u * (2 * STAGES + b); };
+  auto tempty_bar = [&](int b) { return ctrl_addr + 8u * (2 * STAGES + 2 + b); };
+  volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(ctrl + 8 * (2 * STAGES + 4));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(ctrl + 8 * (2 * STAGES + 4) + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);   // the even CTA's producer arrives (with both CTAs' bytes)
+      ptx::mbar_init(empty_bar(s), 1);  // one MMA commit per use
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(tfull_bar(b), 1);
+      ptx::mbar_init(tempty_bar(b), 8);  // one arrival per epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(ptx::smem_u32(const_cast<uint32_t *>(tmem_base_ptr)), TMEM_COLS);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_ptr;
+
+  const int num_tiles = prm.tiles_m * prm.tiles_n;
+  const int num_kb = prm.num_kb;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
+        int mb, nb;
+        gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
+        const int m0 = mb * (2 * BM) + (int)rank * BM;   // this CTA's rows of A
+        const int n0 = nb * BN + (int)rank * BN_CTA;     // this CTA's half of B
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * (A_STAGE_BYTES + B_STAGE_BYTES));
+          const uint32_t fb = ptx::mapa(full_bar(stage), 0);
+          const uint32_t a_dst = a_base + stage * A_STAGE_BYTES, b_dst = b_base + stage * B_STAGE_BYTES;
+          const int k0 = kb * kblock<TI>();
+          if constexpr (EPI == Epilogue::kConv) {
+            const int cb = kb % prm.conv_c_blocks, rs = kb / prm.conv_c_blocks;
+            const int r = rs / prm.conv_s, sx = rs % prm.conv_s;
+            const int img = mb / prm.conv_tiles_img;
+            const int pos0 = (mb % prm.conv_tiles_img) * (2 * BM) + (int)rank * BM;
+            ptx::tma_load_3d_pair(a_dst, &tmap_a, fb, cb * gemm::BK, pos0 + (r - prm.conv_pad_h) * prm.conv_wp + sx,
+                                  img);
+            ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, cb * gemm::BK, rs, n0);
+          } else {
+            ptx::tma_load_2d_pair(a_dst, &tmap_a, fb, k0, m0);
+            if constexpr (B_MN_MAJOR) {
+#pragma unroll
+              for (int j = 0; j < BN_CTA / kblock<TI>(); ++j)
+                ptx::tma_load_2d_pair(b_dst + j * (kblock<TI>() * 128), &tmap_b, fb, n0 + kblock<TI>() * j, k0);
+            } else {
+              ptx::tma_load_2d_pair(b_dst, &tmap_b, fb, k0, n0);
+            }
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+      // Wait until the MMAs have released every stage this CTA filled, so that
+      // no commit arrival is still in flight towards this CTA when it exits.
+      for (int i = 0; i < STAGES && ok; ++i) {
+        if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) ok = false;
+        if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = ptx::f16_idesc(umma_format<TI>(), 0, B_MN_MAJOR ? 1 : 0, 2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += pairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1) & 1u;
+        if (!ptx::mbar_wait(tempty_bar(buf), use ^ 1u, abort_flag)) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const uint32_t a_addr = a_base + stage * A_STAGE_BYTES;
+          const uint32_t b_addr = b_base + stage * B_STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K
+            const uint64_t a_desc = ptx::sw128_desc(a_addr + kk * 32, 16, 1024);
+            uint64_t b_desc;
+            if constexpr (B_MN_MAJOR)
+              b_desc = ptx::sw128_desc(b_addr + kk * mma_k<TI>() * 128, kblock<TI>() * 128, 1024);
+            else
+              b_desc = ptx::sw128_desc(b_addr + kk * 32, 16, 1024);
+            if constexpr (sizeof(TI) == 1)
+              ptx::mma_f8_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              ptx::mma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          ptx::mma_commit_pair_both(empty_bar(stage));
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) ptx::mma_commit_pair_both(tfull_bar(buf));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quarter = warp & 3;  // TMEM lanes this warp may access
+    int local = 0;
+    for (int tile = pair; tile < num_tiles; tile += pairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1) & 1u;
+      if (!ptx::mbar_wait_warp(tfull_bar(buf), use, abort_flag)) break;
+      ptx::tc_fence_after();
+      int mb, nb;
+      gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
+      if constexpr (EPI == Epilogue::kConv)
+        gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
+                                             (int64_t)(mb % prm.conv_tiles_img) * (2 * BM) + rank * BM,
+                                             (int64_t)nb * BN, mb / prm.conv_tiles_img);
+      else
+        gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
+                                             (int64_t)mb * (2 * BM) + rank * BM, (int64_t)nb * BN, 0);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(buf), 0));
+    }
+  }
+
+  __syncwarp();
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // no CTA leaves while its pair may still touch its shared or tensor memory
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm2
+
+// Launches gemm_pair_kernel persistently: as many CTA pairs as can be resident
+// at once (74 on a full B200), or fewer when there are fewer pair tiles.
+template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
+int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params &prm, cudaStream_t stream) {
+  auto kern = gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM_BYTES);
+  if (e != cudaSuccess) return (int)e;
+  static int resident_pairs[64] = {};  // per device, filled on first use
+  int device = 0;
+  cudaGetDevice(&device);
+  int pairs = device < 64 ? resident_pairs[device] : 0;
+  if (pairs == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
+    cfg.blockDim = dim3(gemm2::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = gemm2::SMEM_BYTES;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&pairs, kern, &cfg) != cudaSuccess || pairs <= 0) {
+      cudaGetLastError();
+      pairs = sm_count() / 2;
+    }
+    if (device < 64) resident_pairs[device] = pairs;
+  }
+  const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
+  const int grid_pairs = (int)(tiles < pairs ? tiles : pairs);
+  kern<<<2 * grid_pairs, gemm2::THREADS, gemm2::SMEM_BYTES, stream>>>(ta, tb, prm);
+  return launch_status();
+}
 
 // Launches the tensor-core GEMM when the operands meet its layout rules;
 // returns kNotEligible otherwise so the caller takes the general-layout path.
@@ -374,6 +627,9 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
     if (!aligned16(p.b)) return kNotEligible;
     if (p.K * E < 16 || (b_mn && p.N * E < 16)) return kNotEligible;
 
+    // CTA pairs (256-row tiles) unless A has a single 128-row tile
+    const bool pair = p.M > BM;
+    const uint32_t b_rows = pair ? (uint32_t)gemm2::BN_CTA : (uint32_t)BN;  // B rows staged per CTA
     CUtensorMap ta, tb;
     if (!make_tmap_2d(&ta, p.a, tmap_dtype<TI>(), E, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.sam, KB, BM))
       return kNotEligible;
@@ -381,7 +637,7 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
       if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), E, (uint64_t)p.N, (uint64_t)p.K, (uint64_t)p.sbk, KB, KB))
         return kNotEligible;
     } else {
-      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), E, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.sbn, KB, BN))
+      if (!make_tmap_2d(&tb, p.b, tmap_dtype<TI>(), E, (uint64_t)p.K, (uint64_t)p.N, (uint64_t)p.sbn, KB, b_rows))
         return kNotEligible;
     }
     Params prm{};
@@ -389,11 +645,15 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
     prm.out = p.out; prm.som = p.som; prm.son = p.son;
     prm.bias = p.bias; prm.sim = p.sim; prm.sin = p.sin;
     prm.beta = p.beta; prm.alpha = p.alpha;
-    prm.tiles_m = (int)((p.M + BM - 1) / BM);
+    const int tile_m = pair ? 2 * BM : BM;
+    prm.tiles_m = (int)((p.M + tile_m - 1) / tile_m);
     prm.tiles_n = (int)((p.N + BN - 1) / BN);
     prm.num_kb = (int)((p.K + KB - 1) / KB);
     const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
     if (tiles > (1LL << 30)) return kNotEligible;
+    if (pair)
+      return b_mn ? launch_pair<TI, TO, EPI, true>(ta, tb, prm, stream)
+                  : launch_pair<TI, TO, EPI, false>(ta, tb, prm, stream);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     auto kern = b_mn ? gemm_kernel<TI, TO, EPI, true> : gemm_kernel<TI, TO, EPI, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
@@ -584,6 +844,9 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     }
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return kNotEligible;
+    // CTA pairs (256-position tiles) unless an image has a single 128-position tile
+    const bool pair = p.P * wp > BM;
+    const int tile_m = pair ? 2 * BM : BM;
     CUtensorMap ta, tb;
     {
       // [image][H * Wp rows][C]: one image per outer index, so rows shifted
@@ -600,7 +863,7 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     {
       const cuuint64_t dims[3] = {(cuuint64_t)p.c, (cuuint64_t)(p.r * p.s), (cuuint64_t)p.k};
       const cuuint64_t strides[2] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.r * p.s * p.c * 2)};
-      const cuuint32_t box[3] = {64, 1, (cuuint32_t)BN};
+      const cuuint32_t box[3] = {64, 1, (cuuint32_t)(pair ? gemm2::BN_CTA : BN)};
       const cuuint32_t estr[3] = {1, 1, 1};
       if (fn(&tb, tmap_dtype<T>(), 3, flt, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -613,7 +876,7 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     prm.conv_s = (int)p.s;
     prm.conv_pad_h = (int)p.pad_h;
     prm.conv_wp = (int)wp;
-    prm.conv_tiles_img = (int)((p.P * wp + BM - 1) / BM);
+    prm.conv_tiles_img = (int)((p.P * wp + tile_m - 1) / tile_m);
     prm.conv_P = (int)p.P;
     prm.conv_Q = (int)p.Q;
     prm.conv_osn = p.os[0];
@@ -624,11 +887,12 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     prm.tiles_m = (int)tiles_m;
     prm.tiles_n = (int)((p.k + BN - 1) / BN);
     prm.num_kb = (int)(p.r * p.s * prm.conv_c_blocks);
-    prm.M = tiles_m * BM;
+    prm.M = tiles_m * tile_m;
     prm.N = p.k;
     prm.K = p.r * p.s * p.c;
     const int64_t tiles = tiles_m * prm.tiles_n;
     if (tiles > (1LL << 30)) return kNotEligible;
+    if (pair) return launch_pair<T, T, Epilogue::kConv, false>(ta, tb, prm, stream);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     auto kern = gemm_kernel<T, T, Epilogue::kConv, false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
