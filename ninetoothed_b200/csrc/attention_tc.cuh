@@ -25,7 +25,7 @@
 // While one tile's softmax runs, the tensor cores work on the other tile; an
 // item's epilogue and the next item's Q load overlap the other tile's work.
 // Causal items skip key blocks above the diagonal and are dealt out longest
-// first.  Every mbarrier wait is bounded in time.
+// first, in alternating-direction rounds.  Every mbarrier wait is bounded in time.
 #pragma once
 
 #include <cuda.h>
@@ -144,6 +144,14 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
   };
   // key blocks Q tile t of an item starting at query q0 needs (causal: up to
   // its diagonal block)
+  // The CTA's i-th item: items are dealt to the CTAs in rounds, alternating
+  // direction each round (0..G-1, then G-1..0), which balances the causal
+  // lengths (sorted longest first) far better than plain round-robin.
+  auto nth_item = [&](int i) {
+    const int g = (int)gridDim.x, c = (int)blockIdx.x;
+    const int64_t k = (int64_t)i * g + ((i & 1) ? g - 1 - c : c);
+    return k < num_items ? (int)k : -1;
+  };
   auto n_blk = [&](int q0, int t) {
     return prm.causal ? min(kv_blocks, (q0 + t * BM + BM - 1) / BN + 1) : kv_blocks;
   };
@@ -184,8 +192,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     if (lane == 0) {
       bool ok = true;
       int r = 0;  // ring items issued so far (all work items)
-      int it = 0;
-      for (int k = blockIdx.x; k < num_items && ok; k += gridDim.x, ++it) {
+      for (int it = 0, k = nth_item(0); k >= 0 && ok; k = nth_item(++it)) {
         const Item w = item(k);
         const int n_max = n_blk(w.q0, TILES - 1);
         // Q_t of this item once the previous item's last QK_t has read Q_t
@@ -243,8 +250,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
       bool ok = true;
       int r = 0;                 // ring position of this item's K_0
       int blk[TILES] = {0, 0};   // key blocks of tile t in earlier items (s_full / p_full phases)
-      int it = 0;
-      for (int k = blockIdx.x; k < num_items && ok; k += gridDim.x, ++it) {
+      for (int it = 0, k = nth_item(0); k >= 0 && ok; k = nth_item(++it)) {
         const Item w = item(k);
         const int n0 = n_blk(w.q0, 0), n1 = n_blk(w.q0, 1);
         const int n_max = n1;
@@ -304,8 +310,7 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     bool ok = true;
     int blk = 0;  // key blocks of this tile in earlier items
-    int it = 0;
-    for (int k = blockIdx.x; k < num_items && ok; k += gridDim.x, ++it) {
+    for (int it = 0, k = nth_item(0); k >= 0 && ok; k = nth_item(++it)) {
       const Item w = item(k);
       const int qi = w.q0 + t * BM + row;
       const int n_t = n_blk(w.q0, t);
