@@ -284,8 +284,13 @@ def _make_materializer_class():
             if output_dir is None:
                 source = write_source(name, text, "b200.json", cache_key=compilation_cache_key(compilation))
             else:
+                from ninetoothed_b200 import cpp_export
+
                 source = Path(output_dir) / f"{name}.b200.json"
                 atomic_write_text(source, text)
+                # launch_<kernel> over the reference's C++ tensor ABI, when the
+                # variant's dtypes are static
+                cpp_export.write_sources(compilation, program, compilation.request.specialization_values, output_dir)
             launch = _bind(compilation.launch_abi, program, compilation.request.specialization_values)
             # The handle's manifest goes beside the descriptor (the cache or the
             # AOT output directory), never beside the shared library inside the
