@@ -224,6 +224,44 @@ int nt_b200_conv2d_no_alloc(const void *input, const void *filter, void *output,
                             const int64_t *filter_strides,
                             const int64_t *output_strides, int dtype, void *stream);
 
+/*
+ * clone (tests/test_clone.py:10-47, all four applications): output[i, j] =
+ * input[i, j] for a rows x cols matrix with any element strides; a bit copy
+ * of any dtype code 0-13.
+ */
+int nt_b200_clone(const void *input, void *output, int64_t rows, int64_t cols,
+                  int64_t input_stride_row, int64_t input_stride_col,
+                  int64_t output_stride_row, int64_t output_stride_col, int dtype,
+                  void *stream);
+
+/*
+ * to_padded_tensor (tests/test_jagged.py:12-49): a jagged 3-D tensor with one
+ * ragged dimension -- packed `values` holding element (b, r, d) at
+ * (offsets[b] + r) * values_stride_ragged + d * values_stride_inner, device
+ * `offsets` [batch + 1] (int64), `inner` elements along the dense dimension --
+ * to a dense `output` whose element (b, r, d) sits at output_strides[0] * b +
+ * output_strides[1] * r + output_strides[2] * d for r < max_len; positions
+ * r >= len_b hold `padding` converted to the dtype (codes 0-11).  Ragged
+ * dimension 1: the strides of values [total, D] in order; ragged dimension 2:
+ * values [D, total] with its strides swapped.
+ */
+int nt_b200_jagged_to_padded(const void *values, const int64_t *offsets, int64_t batch,
+                             int64_t inner, int64_t values_stride_ragged,
+                             int64_t values_stride_inner, double padding, void *output,
+                             int64_t max_len, const int64_t *output_strides, int dtype,
+                             void *stream);
+
+/*
+ * Copy with expand into a jagged tensor (tests/test_jagged.py:104-143): every
+ * element (b, r, d) of the jagged tensor (layout as above) becomes
+ * src[b * src_stride_batch + d * src_stride_inner], the dense source being
+ * broadcast along the ragged dimension.  batch <= 65535.
+ */
+int nt_b200_jagged_expand(void *values, const int64_t *offsets, int64_t batch, int64_t inner,
+                          int64_t values_stride_ragged, int64_t values_stride_inner,
+                          const void *src, int64_t src_stride_batch, int64_t src_stride_inner,
+                          int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

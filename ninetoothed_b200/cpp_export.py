@@ -189,6 +189,12 @@ def _body(program, a):
             f"static_cast<int64_t>({a.scalar(2)}), tensor_3.data, {shape(0, 0)}, {stride(0, 0)}, {stride(3, 0)}, "
             f"{code(0)}, stream);",
         ]
+    if program == "clone":
+        return [
+            f"if ({shape(1, 0)} != {shape(0, 0)} || {shape(1, 1)} != {shape(0, 1)}) return {_SHAPE};",
+            f"return nt_b200_clone(tensor_0.data, tensor_1.data, {shape(0, 0)}, {shape(0, 1)}, {stride(0, 0)}, "
+            f"{stride(0, 1)}, {stride(1, 0)}, {stride(1, 1)}, {code(0)}, stream);",
+        ]
     raise NotExportable(f"program {program}")
 
 

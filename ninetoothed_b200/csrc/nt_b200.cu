@@ -7,6 +7,7 @@
 #include "softmax.cuh"
 #include "elementwise.cuh"
 #include "pool.cuh"
+#include "copy.cuh"
 #include "contractions.cuh"
 #include "conv_no_alloc.cu"
 

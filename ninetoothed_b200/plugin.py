@@ -64,6 +64,13 @@ def _ranks(kernel) -> tuple:
     return tuple(int(spec.attrs.get("source_ndim", spec.ndim)) for spec in kernel.tensors)
 
 
+def _store_targets(kernel) -> set:
+    from ninetoothed.backends.emitters import ssa as shared_emitter
+
+    walked = shared_emitter._walk_ops(kernel.ssa.blocks[0].operations)
+    return {op.operands[1] for op in walked if op.opcode == "mem.store" and len(op.operands) == 2}
+
+
 def recognize(kernel) -> str:
     """Name of the B200 program that implements `kernel` (an ir.Kernel after
     the SSA pass pipeline), from its schedule granularity, tensor ranks and
@@ -105,10 +112,32 @@ def recognize(kernel) -> str:
             return "pow"
         if ranks == (1, 0, 0, 1) and ops["math.rand"] == 1 and ops["select.where"] == 1:
             return "dropout"
+    if granularity == "elementwise-grid" and len(ranks) == 2 and ranks[0] == ranks[1] and ops["mem.store"] == 1:
+        # layout programs: the stored value is the other tensor itself, read
+        # directly, through its source, or through pointer arithmetic on it
+        pointer_math = ops["arith.mul"] + ops["arith.add"] > 0
+        if only("arith.mul", "arith.add") and (not pointer_math or (ops["mem.data_ptr"] and ops["tensor.stride"])):
+            specs = kernel.tensors
+            jagged = tuple(getattr(spec, "jagged_dim", None) for spec in specs)
+            stored = _store_targets(kernel)
+            if jagged == (None, None) and ranks == (2, 2) and stored == {specs[1].name}:
+                return "clone"
+            if ranks == (3, 3) and jagged[0] in (1, 2) and jagged[1] is None and not pointer_math:
+                if stored == {specs[1].name}:
+                    return "to_padded"
+                if stored == {specs[0].name}:
+                    return "jagged_expand"
     raise NotImplementedError(
         f"The B200 backend has no kernel for `{kernel.kernel_name}` "
         f"(granularity={granularity}, ranks={ranks}, ops={dict(ops)})."
     )
+
+
+def _constants(program, kernel) -> dict:
+    if program == "to_padded":
+        other = kernel.tensors[0].attrs.get("other")
+        return {"padding": float(other) if other is not None else 0.0}
+    return {}
 
 
 def _is_b200(target_metadata) -> bool:
@@ -195,6 +224,9 @@ def _make_backend_class():
                 "launch_grid": ("1",),
                 "launch_block": (1,),
                 "b200_program": program,
+                # values the program needs that live in the tensor specs
+                # (the padding of to_padded_tensor is its input's `other`)
+                "b200_constants": _constants(program, kernel),
             }
             return Artifact(
                 backend=Target.CUDA,
@@ -222,10 +254,13 @@ def _program_kernel(program):
         "add": programs.add_kernel,
         "pow": programs.pow_kernel,
         "dropout": programs.dropout_kernel,
+        "clone": programs.clone_kernel,
+        "to_padded": programs.to_padded_kernel,
+        "jagged_expand": programs.jagged_expand_kernel,
     }[program]
 
 
-def _bind(compilation_abi, program, specialization=None):
+def _bind(compilation_abi, program, specialization=None, constants=None):
     """Launch closure: the compilation's public arguments, in order, become the
     program kernel's positional arguments.  Meta values the program takes come
     from the call's keywords or, for constexpr symbols the reference runtime
@@ -247,6 +282,7 @@ def _bind(compilation_abi, program, specialization=None):
         # their index maps, which this binding cannot read.
         raise NotImplementedError("max_pool2d arrangements without WINDOW_HEIGHT/WINDOW_WIDTH are not bound")
     fixed_meta = {name: value for name, value in specialization.items() if name in kernel.meta}
+    fixed_meta.update({name: value for name, value in dict(constants or {}).items() if name in kernel.meta})
 
     def launch(*args, **kwargs):
         positional = list(args) + [kwargs.pop(name) for name in public[len(args):] if name in kwargs]
@@ -291,7 +327,8 @@ def _make_materializer_class():
                 # launch_<kernel> over the reference's C++ tensor ABI, when the
                 # variant's dtypes are static
                 cpp_export.write_sources(compilation, program, compilation.request.specialization_values, output_dir)
-            launch = _bind(compilation.launch_abi, program, compilation.request.specialization_values)
+            launch = _bind(compilation.launch_abi, program, compilation.request.specialization_values,
+                           compilation.artifact.metadata.get("b200_constants"))
             # The handle's manifest goes beside the descriptor (the cache or the
             # AOT output directory), never beside the shared library inside the
             # package; the built artifact still names the library it binds.
@@ -316,7 +353,8 @@ def _make_materializer_class():
             from ninetoothed.compiler.runtime import _launch_abi_from_dict
 
             specialization = dict(built.source.metadata.get("kernel_metadata", {})).get("specialization_values", {})
-            return _bind(_launch_abi_from_dict(built.abi), built.source.metadata["b200_program"], specialization)
+            return _bind(_launch_abi_from_dict(built.abi), built.source.metadata["b200_program"], specialization,
+                         built.source.metadata.get("b200_constants"))
 
     return B200Materializer
 

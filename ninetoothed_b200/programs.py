@@ -352,12 +352,128 @@ def dropout(input, p=0.5, seed=None):
     return dropout_kernel(input, p, seed, torch.empty_like(input))
 
 
+# --------------------------------------------------------------------- layout programs
+ALL_DTYPES = tuple(getattr(torch, name) for name in _lib.DTYPE_CODES if hasattr(torch, name))
+
+
+def _launch_clone(v, stream):
+    x, out = v["input"], v["output"]
+    if x.dtype != out.dtype or x.shape != out.shape:
+        raise TypeError("Kernel arguments `input`, `output` must share shape and dtype.")
+    return _lib_call(
+        "nt_b200_clone", ptr(x), ptr(out), x.shape[0], x.shape[1], *x.stride(), *out.stride(), dtype_code(x.dtype),
+        stream,
+    )
+
+
+# tests/test_clone.py:10-47 (any of its four applications): (input, output).
+clone_kernel = Kernel(
+    name="clone",
+    args=(TensorArg("input", 2, ALL_DTYPES), TensorArg("output", 2, ALL_DTYPES)),
+    outputs=("output",),
+    launch=_launch_clone,
+)
+
+
+def clone(input):
+    """tests/test_clone.py:35-47."""
+    return clone_kernel(input, torch.empty_like(input))
+
+
+def _jagged_parts(x, name):
+    """(values, offsets, ragged dim, values stride along it, values stride along
+    the dense dim, dense extent) of a 3-D jagged nested tensor."""
+    if not getattr(x, "is_nested", False):
+        raise TypeError(f"Kernel argument `{name}` must be a jagged nested tensor.")
+    ragged = int(getattr(x, "_ragged_idx", 1))
+    if x.dim() != 3 or ragged not in (1, 2):
+        raise TypeError(f"Kernel argument `{name}` must be 3-D with its ragged dimension at 1 or 2.")
+    values, offsets = x.values(), x.offsets()
+    if offsets.dtype != torch.int64 or not offsets.is_contiguous():
+        offsets = offsets.to(torch.int64).contiguous()
+    dense = 2 - ragged  # the dense dimension of `values`
+    return values, offsets, ragged, values.stride(ragged - 1), values.stride(dense), values.shape[dense]
+
+
+def _launch_to_padded(v, stream):
+    x, out = v["input"], v["output"]
+    if x.dtype != out.dtype:
+        raise TypeError("Kernel arguments `input`, `output` must share one dtype.")
+    values, offsets, ragged, vs_r, vs_d, inner = _jagged_parts(x, "input")
+    batch = offsets.numel() - 1
+    if out.shape[0] != batch or out.shape[3 - ragged] != inner:
+        raise TypeError("to_padded_tensor output extents disagree with the input.")
+    os_ = _lib.int64_array((out.stride(0), out.stride(ragged), out.stride(3 - ragged)))
+    return _lib_call(
+        "nt_b200_jagged_to_padded", ptr(values), ptr(offsets), batch, inner, vs_r, vs_d, float(v["padding"]),
+        ptr(out), out.shape[ragged], os_, dtype_code(out.dtype), stream,
+    )
+
+
+# tests/test_jagged.py:12-49: (input, output); the padding is the jagged
+# input's `other`, fixed when the program is built.
+to_padded_kernel = Kernel(
+    name="to_padded",
+    args=(TensorArg("input", 3, ALL_DTYPES), TensorArg("output", 3, ALL_DTYPES)),
+    outputs=("output",),
+    launch=_launch_to_padded,
+    meta=("padding",),
+    meta_defaults={"padding": 0.0},
+)
+
+
+def to_padded_tensor(input, padding):
+    """tests/test_jagged.py:37-49."""
+    ragged = int(getattr(input, "_ragged_idx", 1))
+    offsets = input.offsets()
+    max_len = int(offsets.diff().max().item()) if offsets.numel() > 1 else 0
+    shape = tuple(max_len if dim == ragged else size for dim, size in enumerate(input.shape))
+    output = torch.empty(shape, dtype=input.dtype, device=input.device)
+    return to_padded_kernel(input, output, padding=padding)
+
+
+def _launch_jagged_expand(v, stream):
+    dst, src = v["dst"], v["src"]
+    if dst.dtype != src.dtype:
+        raise TypeError("Kernel arguments `dst`, `src` must share one dtype.")
+    values, offsets, ragged, vs_r, vs_d, inner = _jagged_parts(dst, "dst")
+    batch = offsets.numel() - 1
+    if src.shape[0] != batch or src.shape[ragged] != 1 or src.shape[3 - ragged] != inner:
+        raise TypeError("copy source extents disagree with the jagged destination.")
+    return _lib_call(
+        "nt_b200_jagged_expand", ptr(values), ptr(offsets), batch, inner, vs_r, vs_d, ptr(src), src.stride(0),
+        src.stride(3 - ragged), dtype_code(dst.dtype), stream,
+    )
+
+
+# tests/test_jagged.py:104-143: copy(dst, src) with src expanded along the
+# jagged dimension.
+jagged_expand_kernel = Kernel(
+    name="jagged_expand",
+    args=(TensorArg("dst", 3, ALL_DTYPES), TensorArg("src", 3, ALL_DTYPES)),
+    outputs=("dst",),
+    launch=_launch_jagged_expand,
+)
+
+
+def copy(dst, src):
+    """tests/test_jagged.py:139-143."""
+    return jagged_expand_kernel(dst, src)
+
+
 __all__ = [
     "KernelLaunchError",
     "add",
     "add_kernel",
     "addmm",
     "addmm_kernel",
+    "ALL_DTYPES",
+    "clone",
+    "clone_kernel",
+    "copy",
+    "jagged_expand_kernel",
+    "to_padded_kernel",
+    "to_padded_tensor",
     "attention",
     "attention_kernel",
     "conv2d",

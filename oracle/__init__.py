@@ -197,3 +197,37 @@ def philox_word(offset: int, seed: int) -> int:
 
 def uniform(word: int) -> float:
     return float(_library().oracle_uniform(word))
+
+
+# ----------------------------------------------------------------- layout programs
+# Pure data movement: numpy restatements (every element is moved bit for bit).
+
+
+def clone(x) -> np.ndarray:
+    """tests/test_clone.py:10-47: output[i, j] = input[i, j] for any strides
+    (all four of its applications compute this)."""
+    return np.array(x, copy=True)
+
+
+def to_padded(values, offsets, padding, max_len) -> np.ndarray:
+    """tests/test_jagged.py:12-49: a jagged [B, (len_b), D] tensor (packed
+    `values` [total, D], `offsets` [B + 1]) -> dense [B, max_len, D], rows past
+    len_b filled with `padding` (the jagged input's `other`)."""
+    values = np.asarray(values)
+    offsets = np.asarray(offsets, dtype=np.int64)
+    batch = len(offsets) - 1
+    out = np.full((batch, max_len) + values.shape[1:], padding, dtype=values.dtype)
+    for b in range(batch):
+        n = min(int(offsets[b + 1] - offsets[b]), max_len)
+        out[b, :n] = values[offsets[b]:offsets[b] + n]
+    return out
+
+
+def jagged_expand(src, offsets) -> np.ndarray:
+    """tests/test_jagged.py:104-181: dst[b, i, ...] = src[b, 0, ...] for every
+    row i of batch b of a jagged dst; returns dst's packed values [total, ...]."""
+    src = np.asarray(src)
+    offsets = np.asarray(offsets, dtype=np.int64)
+    rows = [np.broadcast_to(src[b, 0], (int(offsets[b + 1] - offsets[b]),) + src.shape[2:])
+            for b in range(len(offsets) - 1)]
+    return np.concatenate(rows, axis=0) if rows else np.zeros((0,) + src.shape[2:], dtype=src.dtype)

@@ -56,6 +56,8 @@ import tests.test_dropout as ref_dropout  # noqa: E402
 import tests.test_matmul as ref_matmul  # noqa: E402
 import tests.test_max_pool2d as ref_max_pool2d  # noqa: E402
 import tests.test_softmax as ref_softmax  # noqa: E402
+import tests.test_clone as ref_clone  # noqa: E402
+import tests.test_jagged as ref_jagged  # noqa: E402
 
 
 def save(name, **arrays):
@@ -210,6 +212,34 @@ def gen_elementwise(g):
         save(tag, input=np16(x), p=p, seed=seed, output=np16(out))
 
 
+def gen_clone(g):
+    # the reference's four clone applications (direct, pointer arithmetic,
+    # source indexing, store through the source) on a row-padded input
+    x = torch.empty_strided((65, 40), (70, 1))
+    x.copy_(torch.randn(65, 40, generator=g))
+    for impl_id, application in enumerate(ref_clone.applications):
+        out = torch.empty(65, 40)
+        kernel = ninetoothed.make(ref_clone.arrangement, application, (Tensor(2), Tensor(2)), max_num_configs=1)
+        kernel(x, out)
+        save(f"clone_f32_65x40_impl{impl_id}", input=np16(x), input_strides=x.stride(), output=np16(out))
+
+
+def gen_jagged(g):
+    # to_padded_tensor and the broadcast copy into a jagged tensor
+    # (tests/test_jagged.py), jagged dim 1, float32 and float16
+    lengths = (5, 17, 1, 9)
+    for dtype, tag in ((torch.float32, "f32"), (torch.float16, "f16")):
+        batches = [torch.randn(n, 24, generator=g).to(dtype) for n in lengths]
+        x = torch.nested.nested_tensor(batches, layout=torch.jagged)
+        out = ref_jagged.to_padded_tensor(x, padding=-1, jagged_dim=1, block_size=16)
+        save(f"to_padded_{tag}_b4_d24", values=np16(x.values()), offsets=np16(x.offsets()), padding=-1.0,
+             output=np16(out))
+        src = torch.randn(len(lengths), 1, 24, generator=g).to(dtype)
+        dst = torch.nested.nested_tensor([torch.zeros(n, 24, dtype=dtype) for n in lengths], layout=torch.jagged)
+        ref_jagged.copy(dst, src, 1, block_size=16)
+        save(f"jagged_expand_{tag}_b4_d24", src=np16(src), offsets=np16(dst.offsets()), output=np16(dst.values()))
+
+
 if __name__ == "__main__":
     g = torch.Generator().manual_seed(20261201)
     which = set(sys.argv[1:])
@@ -221,6 +251,8 @@ if __name__ == "__main__":
         ("matmul", gen_matmul),
         ("attention", gen_attention),
         ("conv2d", gen_conv2d),
+        ("clone", gen_clone),
+        ("jagged", gen_jagged),
     ):
         if not which or name in which:
             fn(g)

@@ -1,0 +1,111 @@
+"""GPU parity of the layout programs (clone, to_padded_tensor, copy into a
+jagged tensor) against the CPU oracle and the reference's golden fixtures.
+All three move bits, so every comparison is exact."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from ninetoothed_b200 import programs
+from tests import golden_io
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _bits(t):
+    """numpy view of a tensor's bits (numpy has no bfloat16)."""
+    t = t.detach().cpu()
+    return t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+@pytest.mark.parametrize("name", golden_io.names("clone_"))
+def test_clone_matches_reference_fixture(name):
+    g = golden_io.load(name)
+    t = torch.from_numpy(np.ascontiguousarray(g["input"]))
+    x = torch.empty_strided(t.shape, tuple(int(s) for s in g["input_strides"]), dtype=t.dtype, device=DEV)
+    x.copy_(t.to(DEV))
+    got = programs.clone(x)
+    np.testing.assert_array_equal(got.cpu().numpy(), g["output"])
+
+
+@pytest.mark.parametrize("dtype", programs.ALL_DTYPES, ids=str)
+def test_clone_every_dtype_bit_exact(dtype):
+    gen = torch.Generator(device=DEV).manual_seed(3)
+    raw = torch.randint(0, 256, (257, 8 * 131), device=DEV, generator=gen, dtype=torch.uint8)
+    x = raw.view(dtype)
+    x = x[:, 1: x.shape[1] - 2]  # row-padded, rows not 16-byte aligned
+    got = programs.clone(x)
+    assert torch.equal(got.contiguous().view(torch.uint8), x.contiguous().view(torch.uint8))
+
+
+@pytest.mark.parametrize(
+    "shape, in_strides, out_strides",
+    [
+        ((641, 280), (700, 300), (280, 1)),     # the reference test's overlapping strides
+        ((300, 200), (1, 300), (200, 1)),       # column-major -> row-major
+        ((300, 200), (200, 1), (1, 300)),       # row-major -> column-major
+        ((1, 1000), (5000, 3), (1000, 1)),      # one strided row
+        ((1000, 1), (7, 1), (1, 1)),            # one column
+        ((33, 65), (65, 1), (65, 1)),           # dense, odd extents
+    ],
+)
+def test_clone_strides(shape, in_strides, out_strides):
+    def span(strides):
+        return sum((n - 1) * s for n, s in zip(shape, strides)) + 1
+
+    x = torch.as_strided(torch.randn(span(in_strides), device=DEV), shape, in_strides)
+    out = torch.as_strided(torch.full((span(out_strides),), float("nan"), device=DEV), shape, out_strides)
+    programs.clone_kernel(x, out)
+    assert torch.equal(out, x)
+
+
+@pytest.mark.parametrize("name", golden_io.names("to_padded_"))
+def test_to_padded_matches_reference_fixture(name):
+    g = golden_io.load(name)
+    values = torch.from_numpy(g["values"]).to(DEV)
+    offsets = g["offsets"]
+    x = torch.nested.nested_tensor([values[offsets[b]:offsets[b + 1]] for b in range(len(offsets) - 1)],
+                                   layout=torch.jagged)
+    got = programs.to_padded_tensor(x, float(g["padding"]))
+    np.testing.assert_array_equal(got.cpu().numpy(), g["output"])
+
+
+@pytest.mark.parametrize("name", golden_io.names("jagged_expand_"))
+def test_jagged_expand_matches_reference_fixture(name):
+    g = golden_io.load(name)
+    src = torch.from_numpy(g["src"])
+    lengths = np.diff(g["offsets"])
+    dst = torch.nested.nested_tensor([torch.zeros(int(n), src.shape[2], dtype=src.dtype, device=DEV) for n in lengths],
+                                     layout=torch.jagged)
+    programs.copy(dst, src.to(DEV))
+    np.testing.assert_array_equal(dst.values().cpu().numpy(), g["output"])
+
+
+@pytest.mark.parametrize("ragged", (1, 2))
+@pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.int8, torch.float64))
+def test_jagged_both_ragged_dims_against_oracle(ragged, dtype):
+    gen = torch.Generator().manual_seed(ragged)
+    lengths = [1, 37, 5, 130] if ragged == 1 else [3, 1, 64]
+    inner = 19
+    comps = [(torch.randn((n, inner) if ragged == 1 else (inner, n), generator=gen) * 10).to(dtype) for n in lengths]
+    x = torch.nested.nested_tensor([c.to(DEV) for c in comps], layout=torch.jagged)
+    if int(x._ragged_idx) != ragged:
+        pytest.skip("torch placed the ragged dimension elsewhere")
+    padded = programs.to_padded_tensor(x, -1.0)
+    offsets = np.concatenate([[0], np.cumsum(lengths)])
+    rows = np.concatenate([_bits(c if ragged == 1 else c.t()) for c in comps], axis=0)
+    pad = _bits(torch.tensor(-1.0).to(dtype).reshape(1))[0]
+    expected = oracle.to_padded(rows, offsets, pad, max(lengths))
+    if ragged == 2:
+        expected = expected.transpose(0, 2, 1)
+    np.testing.assert_array_equal(_bits(padded), expected)
+
+    src_shape = (len(lengths), 1, inner) if ragged == 1 else (len(lengths), inner, 1)
+    src = (torch.randn(src_shape, generator=gen) * 10).to(dtype)
+    programs.copy(x, src.to(DEV))
+    got_rows = np.concatenate([_bits(c if ragged == 1 else c.t()) for c in x.unbind()], axis=0)
+    src_rows = _bits(src) if ragged == 1 else _bits(src).transpose(0, 2, 1)
+    np.testing.assert_array_equal(got_rows, oracle.jagged_expand(src_rows, offsets))

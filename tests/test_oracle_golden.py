@@ -105,7 +105,8 @@ def test_uniform_mapping_edges():
 
 
 def test_golden_fixtures_present():
-    for prefix in ("matmul_", "addmm_", "attention_", "conv2d_", "max_pool2d_", "softmax_", "add_", "pow_", "dropout_"):
+    for prefix in ("matmul_", "addmm_", "attention_", "conv2d_", "max_pool2d_", "softmax_", "add_", "pow_", "dropout_",
+                   "clone_", "to_padded_", "jagged_expand_"):
         assert golden_io.names(prefix), prefix
 
 
@@ -119,3 +120,22 @@ def test_fp8_rounding_matches_torch(name):
     ref = x.to(dtype).float().numpy()
     got = np.array([oracle.round_to(name, float(v)) for v in x.numpy()], dtype=np.float32)
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.parametrize("name", golden_io.names("clone_"))
+def test_clone_bit_exact(name):
+    g = golden_io.load(name)
+    np.testing.assert_array_equal(oracle.clone(g["input"]), g["output"])
+
+
+@pytest.mark.parametrize("name", golden_io.names("to_padded_"))
+def test_to_padded_bit_exact(name):
+    g = golden_io.load(name)
+    got = oracle.to_padded(g["values"], g["offsets"], float(g["padding"]), g["output"].shape[1])
+    np.testing.assert_array_equal(got, g["output"])
+
+
+@pytest.mark.parametrize("name", golden_io.names("jagged_expand_"))
+def test_jagged_expand_bit_exact(name):
+    g = golden_io.load(name)
+    np.testing.assert_array_equal(oracle.jagged_expand(g["src"], g["offsets"]), g["output"])

@@ -256,3 +256,53 @@ def test_reference_test_suite_on_b200(nt, monkeypatch, module, params):
     monkeypatch.setenv("NINETOOTHED_PLATFORM", "nvidia-b200")
     test_module = ref.load(module)
     test_module.test(device="cuda", **params)
+
+
+# The reference's layout-program tests (tests/test_clone.py, tests/test_jagged.py),
+# called by their own names and parameters.
+NAMED_REFERENCE_CASES = [
+    *[("test_clone", "test_clone", dict(impl_id=i, size_m=641, size_n=280, stride_m=700, stride_n=300))
+      for i in range(4)],
+    *[("test_jagged", "test_to_padded_tensor", dict(ndim=3, jagged_dim=d, num_batches=b, padding=-1))
+      for d in (1, 2) for b in (2, 3, 7, 16)],
+    *[("test_jagged", "test_expand", dict(ndim=3, jagged_dim=d, num_batches=b)) for d in (1, 2) for b in (2, 3, 7, 16)],
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("module, function, params", NAMED_REFERENCE_CASES,
+                         ids=lambda v: v if isinstance(v, str) else "")
+def test_reference_layout_tests_on_b200(nt, monkeypatch, module, function, params):
+    monkeypatch.setenv("NINETOOTHED_BACKEND", "cuda")
+    monkeypatch.setenv("NINETOOTHED_PLATFORM", "nvidia-b200")
+    getattr(ref.load(module), function)(device="cuda", **params)
+
+
+@pytest.mark.parametrize("impl_id", range(4))
+def test_clone_applications_are_recognised(nt, impl_id):
+    from ninetoothed import Tensor
+
+    cl = ref.load("test_clone")
+    compilation = _compile(nt, cl.arrangement, cl.applications[impl_id], (Tensor(2), Tensor(2)))
+    assert compilation.artifact.metadata["b200_program"] == "clone"
+
+
+def test_jagged_programs_are_recognised(nt):
+    jg = ref.load("test_jagged")
+    for premake, program in ((jg.ToPaddedTensor.premake(3, -1, 1), "to_padded"), (jg.Copy.premake(3, 1), "jagged_expand")):
+        compilation = _compile(nt, *premake)
+        assert compilation.artifact.metadata["b200_program"] == program
+    padded = _compile(nt, *jg.ToPaddedTensor.premake(3, -7, 2))
+    assert padded.artifact.metadata["b200_constants"] == {"padding": -7.0}
+
+
+def test_scaled_copy_is_not_a_clone(nt):
+    from ninetoothed import Tensor
+
+    cl = ref.load("test_clone")
+
+    def application(input, output):
+        output = input * 2  # noqa: F841
+
+    with pytest.raises(NotImplementedError):
+        _compile(nt, cl.arrangement, application, (Tensor(2), Tensor(2)))
