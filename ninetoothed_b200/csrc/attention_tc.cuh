@@ -24,8 +24,9 @@
 //              to the next item) and store O / l to global memory.
 // While one tile's softmax runs, the tensor cores work on the other tile; an
 // item's epilogue and the next item's Q load overlap the other tile's work.
-// Causal items skip key blocks above the diagonal and are dealt out longest
-// first, in alternating-direction rounds.  Every mbarrier wait is bounded in time.
+// Items are dealt out head by head in alternating-direction rounds (causal:
+// longest first within a round); causal items skip key blocks above the
+// diagonal.  Every mbarrier wait is bounded in time.
 #pragma once
 
 #include <cuda.h>
@@ -130,28 +131,43 @@ attention_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_consta
   const int num_items = heads * per_head;
   const int kv_blocks = (prm.SK + BN - 1) / BN;
 
-  // Work item k = (batch, head, pair of Q tiles).  Causal: the pair index is
-  // the slow coordinate, last (longest) pairs of every head first, so each
-  // CTA's round-robin share of the items is balanced and short items fill
-  // the tail.
+  // Work item k = (batch, head, pair of Q tiles), head-major: k = bh *
+  // per_head + pair.  Items are dealt in rounds of G = gridDim.x consecutive
+  // items (about G / per_head heads, whose K and V then stay in L2 while the
+  // round's CTAs stream them), alternating the direction each round (CTA c
+  // takes the round's c-th item, then its (G-1-c)-th).  Causal items differ in
+  // length, so within a round they are taken longest pair first: with the
+  // alternating direction every CTA's share of the work comes out nearly equal.
   struct Item {
     int b, h, q0;
   };
   auto item = [&](int k) {
-    const int bh = prm.causal ? k % heads : k / per_head;
-    const int qp = prm.causal ? per_head - 1 - k / heads : k % per_head;
+    const int bh = k / per_head, qp = k % per_head;
     return Item{bh / prm.H, bh % prm.H, qp * (TILES * BM)};
+  };
+  // p-th item of round w in order of decreasing pair index (ties by k).
+  auto round_item = [&](int w, int p) {
+    const int lo = w * (int)gridDim.x;
+    const int hi = min(lo + (int)gridDim.x, num_items);
+    if (!prm.causal) return lo + p;
+    for (int v = per_head - 1; v >= 0; --v) {
+      const int first = lo + ((v - lo) % per_head + per_head) % per_head;  // first k >= lo with k % per_head == v
+      const int count = first >= hi ? 0 : (hi - 1 - first) / per_head + 1;
+      if (p < count) return first + p * per_head;
+      p -= count;
+    }
+    return -1;
+  };
+  // The CTA's i-th item, or -1 when it has none left.
+  auto nth_item = [&](int i) {
+    const int g = (int)gridDim.x, c = (int)blockIdx.x;
+    if ((int64_t)i * g >= num_items) return -1;
+    const int size = min(g, num_items - i * g);
+    const int p = (i & 1) ? g - 1 - c : c;
+    return p < size ? round_item(i, p) : -1;
   };
   // key blocks Q tile t of an item starting at query q0 needs (causal: up to
   // its diagonal block)
-  // The CTA's i-th item: items are dealt to the CTAs in rounds, alternating
-  // direction each round (0..G-1, then G-1..0), which balances the causal
-  // lengths (sorted longest first) far better than plain round-robin.
-  auto nth_item = [&](int i) {
-    const int g = (int)gridDim.x, c = (int)blockIdx.x;
-    const int64_t k = (int64_t)i * g + ((i & 1) ? g - 1 - c : c);
-    return k < num_items ? (int)k : -1;
-  };
   auto n_blk = [&](int q0, int t) {
     return prm.causal ? min(kv_blocks, (q0 + t * BM + BM - 1) / BN + 1) : kv_blocks;
   };
