@@ -262,6 +262,16 @@ int nt_b200_jagged_expand(void *values, const int64_t *offsets, int64_t batch, i
                           const void *src, int64_t src_stride_batch, int64_t src_stride_inner,
                           int dtype, void *stream);
 
+/*
+ * Failure-detection self-test (no counterpart in the reference): launches one
+ * thread that waits on an mbarrier nothing ever arrives on, through the same
+ * bounded wait the pipelined kernels use, with a limit of `limit_ns`
+ * (1 us .. 1 s).  The wait gives up, records NT_B200_ERR_DEVICE_TIMEOUT in the
+ * device error word and the kernel exits; nt_b200_device_status then reports
+ * it.  The context stays usable.
+ */
+int nt_b200_wait_timeout_selftest(int64_t limit_ns, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

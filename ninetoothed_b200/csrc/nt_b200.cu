@@ -69,3 +69,26 @@ extern "C" int nt_b200_device_status(void *stream, int *status) {
   *status = host;
   return 0;
 }
+
+// Self-test of the bounded waits: one thread waits on an mbarrier that nothing
+// ever arrives on, with a short limit, so the wait runs out the same way a
+// broken pipeline's would.
+namespace nt {
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(&bar), 1);
+    abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ptx::mbar_wait(ptx::smem_u32(&bar), 0, &abort_flag, limit_ns);
+}
+}  // namespace nt
+
+extern "C" int nt_b200_wait_timeout_selftest(int64_t limit_ns, void *stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000LL) return NT_B200_ERR_INVALID_ARGUMENT;
+  nt::wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>((uint64_t)limit_ns);
+  return nt::launch_status();
+}

@@ -54,15 +54,17 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;
 
 // Waits until the barrier's phase with the given parity has completed.
 // Returns false (and raises the CTA's abort flag and the device error word)
-// when the wait runs past kWaitLimitNs or another warp of the CTA aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+// when the wait runs past `limit_ns` (kWaitLimitNs unless a caller such as
+// the wait self-test passes a shorter one) or another warp of the CTA aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         record_error(NT_B200_ERR_DEVICE_TIMEOUT);
         return false;
