@@ -349,6 +349,23 @@ def test_attention_ragged_seq_and_head_dim():
         np.testing.assert_allclose(_np(o), ref, rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("sq, sk, d", [(700, 650, 128), (1000, 1300, 96), (513, 513, 128), (4096, 300, 128)])
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_attention_ragged_items(sq, sk, d, dtype):
+    # partial 256-query work items, key tails shorter and longer than the
+    # queries, causal diagonals, head_dim padded to 128
+    gen = torch.Generator().manual_seed(sq + sk + d)
+    q = torch.randn(2, 3, sq, d, generator=gen).to(dtype)
+    k = torch.randn(2, 3, sk, d, generator=gen).to(dtype)
+    v = torch.randn(2, 3, sk, d, generator=gen).to(dtype)
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    for causal in (False, True):
+        o = programs.attention(q.to(DEV), k.to(DEV), v.to(DEV), is_causal=causal)
+        sel = (slice(1, 2), slice(0, 2))
+        ref = oracle.attention(q[sel], k[sel], v[sel], causal, name, block_n=64)
+        np.testing.assert_allclose(_np(o[sel]), ref, rtol=1e-2, atol=1e-2)
+
+
 # ----------------------------------------------------------------- conv2d
 @pytest.mark.parametrize("padding", (0, (1, 1), (0, 1), (2, 0)))
 def test_conv2d_reference_case(padding):
