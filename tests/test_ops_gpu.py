@@ -400,3 +400,17 @@ def test_conv2d_baseline_config_sampled_images():
         ref = oracle.conv2d(x[sl], w, (1, 1), "float16")
         bound = oracle.conv2d(x[sl].abs(), w.abs(), (1, 1), "float32")
         assert_within_steps(_np(y[sl]), ref, torch.float16, abs_sum=bound)
+
+
+@pytest.mark.parametrize("rows, cols, chunks", [(4096, 4096, 8), (1000, 781, 3), (5, 256, 8), (1, 64, 1)])
+def test_softmax_host_streaming_matches_device_softmax(rows, cols, chunks):
+    # host in, host out, rows streamed in chunks over two CUDA streams
+    gen = torch.Generator().manual_seed(rows)
+    x = (torch.randn(rows, cols, generator=gen) * 2).half().pin_memory()
+    out = programs.softmax_host(x, chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    expected = programs.softmax(x.to(DEV)).cpu()
+    assert torch.equal(out, expected)
+    again = programs.softmax_host(x, out, chunks=chunks)  # reuse of the output buffer
+    torch.cuda.current_stream().synchronize()
+    assert again is out and torch.equal(out, expected)
