@@ -196,7 +196,10 @@ def test_max_pool2d_golden(name):
 
 # ----------------------------------------------------------------- matmul / addmm
 @pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
-@pytest.mark.parametrize("mnk", ((512, 512, 512), (1000, 520, 264), (128, 256, 64), (1, 256, 64), (300, 40, 24)))
+@pytest.mark.parametrize("mnk", ((512, 512, 512), (1000, 520, 264), (128, 256, 64), (1, 256, 64), (300, 40, 24),
+                                 # CTA-pair edges: a second CTA with one row, a second pair tile
+                                 # with one row, the smallest N and K, N past one 256-wide tile
+                                 (129, 256, 64), (257, 264, 72), (640, 8, 8), (384, 520, 1000)))
 def test_matmul_against_oracle(dtype, mnk):
     m, n, k = mnk
     a = torch.randn((m, k)).to(dtype)
@@ -400,6 +403,26 @@ def test_conv2d_baseline_config_sampled_images():
         ref = oracle.conv2d(x[sl], w, (1, 1), "float16")
         bound = oracle.conv2d(x[sl].abs(), w.abs(), (1, 1), "float32")
         assert_within_steps(_np(y[sl]), ref, torch.float16, abs_sum=bound)
+
+
+@pytest.mark.parametrize(
+    "nchw, k, rs, pad, dtype",
+    [
+        ((3, 16, 8, 8), 32, (3, 3), (1, 1), torch.float16),      # 80 positions: one-CTA tiles
+        ((2, 72, 12, 12), 320, (3, 3), (1, 1), torch.bfloat16),  # 168 positions: one pair tile, 2 N tiles, C % 64
+        ((2, 64, 20, 23), 64, (5, 5), (2, 2), torch.float16),    # 5x5 taps, odd width
+        ((1, 8, 40, 40), 16, (1, 1), (0, 0), torch.float16),     # 1x1 filter, no padding
+    ],
+)
+def test_conv2d_tile_and_tap_edges(nchw, k, rs, pad, dtype):
+    gen = torch.Generator().manual_seed(sum(nchw) + k)
+    x = torch.randn(nchw, generator=gen).to(dtype)
+    w = (torch.randn((k, nchw[1]) + rs, generator=gen) * 0.1).to(dtype)
+    y = programs.conv2d(x.to(DEV), w.to(DEV), padding=pad)
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    ref = oracle.conv2d(x, w, pad, name)
+    bound = oracle.conv2d(x.abs(), w.abs(), pad, "float32")
+    assert_within_steps(_np(y), ref, dtype, abs_sum=bound)
 
 
 @pytest.mark.parametrize("rows, cols, chunks", [(4096, 4096, 8), (1000, 781, 3), (5, 256, 8), (1, 64, 1)])
