@@ -475,7 +475,13 @@ def run_b200(args, dist):
     for i in range(3):
         e2e_step(i)
     dist.barrier()
-    e2e_ms = dist.max(time_launches(e2e_step, e2e_steps, stream)) / e2e_steps
+    # three timed runs, the median kept: the host and its PCIe links are shared
+    # with other jobs on this machine, and one disturbed run should not set it
+    e2e_runs = []
+    for _ in range(3):
+        dist.barrier()
+        e2e_runs.append(dist.max(time_launches(e2e_step, e2e_steps, stream)) / e2e_steps)
+    e2e_ms = sorted(e2e_runs)[1]
     e2e_value = SOFTMAX_BYTES * dist.world / (e2e_ms * 1e-3) / 1e9
 
     which = set()
@@ -513,7 +519,8 @@ def run_b200(args, dist):
             },
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": ROWS * COLS * 2,
-                    "d2h_bytes_per_step": ROWS * COLS * 2, "ms_per_step": e2e_ms},
+                    "d2h_bytes_per_step": ROWS * COLS * 2, "ms_per_step": e2e_ms,
+                    "runs_ms_per_step": e2e_runs, "api": "programs.softmax_host"},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "device_error_word": status,
