@@ -305,9 +305,10 @@ def bench_ops(which, steps, dist, peaks):
             achieved = work / (ms * 1e-3) / 1e9
         profile = {"addmm": "gemm", "matmul": "gemm", "attention": "attention", "conv2d": "conv2d",
                    "max_pool2d": "max_pool2d"}[name.split("_")[0] if not name.startswith("max_pool2d") else "max_pool2d"]
+        profile = profile if traffic else None
         results[name] = {"value": achieved * dist.world, "per_gpu": achieved, "unit": unit, "ms": ms,
                          "frac": achieved / peak, "peak": peak,
-                         "traffic": profile_traffic(profile) if traffic else None}
+                         "traffic": profile_traffic(profile) if profile else None}
 
     s = 8192
     if "addmm" in which or "matmul" in which:
@@ -347,6 +348,14 @@ def bench_ops(which, steps, dist, peaks):
             record("conv2d_fp16_n64", lambda i: programs.conv2d_kernel(xs[i % 2], w, ys[i % 2], padding_h=1,
                                                                        padding_w=1),
                    flops, "TFLOP/s", peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2)
+            # conv2d + max_pool2d in one call, as two kernels (the default)
+            # and with the pool inside the conv kernel; work counted as the
+            # conv's FLOPs, so the figures compare directly with conv2d_fp16_n64
+            for tag, inside in (("", False), ("_in_conv_kernel", True)):
+                record("conv2d_max_pool2d" + tag + "_fp16_n64",
+                       lambda i, inside=inside: programs.conv2d_max_pool2d(xs[i % 2], w, padding=1,
+                                                                           pool_in_conv_kernel=inside),
+                       flops, "TFLOP/s", peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2, traffic=False)
         if "max_pool2d" in which:
             for y in ys:
                 programs.conv2d_kernel(xs[0], w, y, padding_h=1, padding_w=1)

@@ -193,6 +193,34 @@ int nt_b200_conv2d(const void *input, const void *filter, void *output, int64_t 
                    void *workspace, int64_t workspace_bytes, int dtype, void *stream);
 
 /*
+ * conv2d followed by max_pool2d with a 3x3 window, stride 2, padding 1 (floor
+ * mode): output[n, k, i, j] = max_pool2d(conv2d(input, filter, padding))[n, k,
+ * i, j], bit-identical to the two programs run one after the other
+ * (nt_b200_conv2d, then nt_b200_max_pool2d), output [n, k, P2, Q2] with
+ * P2 = (P - 1) / 2 + 1, Q2 = (Q - 1) / 2 + 1 for the conv extents P, Q.  The
+ * conv result goes to the workspace.  pool_in_conv_kernel = 0 pools it with
+ * the max_pool2d kernel after the conv kernel (the faster order on B200);
+ * pool_in_conv_kernel = 1 pools inside the tensor-core conv kernel where the
+ * shape allows (extra pool warps per CTA read each pool row back from L2 once
+ * the warp that completes its last input rows hands it over) and falls back to
+ * the two kernels elsewhere.  `workspace` (256-byte aligned) must hold
+ * nt_b200_conv2d_max_pool2d_workspace_size(...) bytes (conv staging + the conv
+ * result + counters).  No single program of the reference does this; it
+ * composes its conv2d and max_pool2d programs (tests/test_conv2d.py,
+ * tests/test_max_pool2d.py).
+ */
+int nt_b200_conv2d_max_pool2d(const void *input, const void *filter, void *output,
+                              int64_t n, int64_t c, int64_t h, int64_t w, int64_t k,
+                              int64_t r, int64_t s, int64_t pad_h, int64_t pad_w,
+                              const int64_t *input_strides, const int64_t *filter_strides,
+                              const int64_t *output_strides, void *workspace,
+                              int64_t workspace_bytes, int pool_in_conv_kernel, int dtype,
+                              void *stream);
+int64_t nt_b200_conv2d_max_pool2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w,
+                                                 int64_t k, int64_t r, int64_t s,
+                                                 int64_t pad_h, int64_t pad_w, int dtype);
+
+/*
  * Workspace bytes the tensor-core conv2d path needs for this problem (0 when
  * the path does not apply: 32-bit dtype or channels not a multiple of 8): the
  * input as NHWC with pad_w zero columns on each side of every row, then the

@@ -84,6 +84,8 @@ SIGNATURES = {
     "nt_b200_jagged_to_padded": (ctypes.c_int, (_P, _P, _I, _I, _I, _I, ctypes.c_double, _P, _I, _PI64, _C, _P)),
     "nt_b200_jagged_expand": (ctypes.c_int, (_P, _P, _I, _I, _I, _I, _P, _I, _I, _C, _P)),
     "nt_b200_wait_timeout_selftest": (ctypes.c_int, (_I, _P)),
+    "nt_b200_conv2d_max_pool2d": (ctypes.c_int, (_P, _P, _P) + (_I,) * 9 + (_PI64, _PI64, _PI64, _P, _I, _C, _C, _P)),
+    "nt_b200_conv2d_max_pool2d_workspace_size": (ctypes.c_int64, (_I,) * 9 + (_C,)),
     "nt_b200_conv2d_workspace_size": (ctypes.c_int64, (_I, _I, _I, _I, _I, _I, _I, _I, _I, _C)),
     "nt_b200_conv2d_no_alloc": (
         ctypes.c_int,

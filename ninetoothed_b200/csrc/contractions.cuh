@@ -143,6 +143,80 @@ extern "C" int64_t nt_b200_conv2d_workspace_size(int64_t n, int64_t c, int64_t h
   return nt::tc::conv_workspace_bytes(n, c, h, w, k, r, s, pad_w, 2);
 }
 
+// conv2d followed by max_pool2d 3x3 / stride 2 / padding 1 (floor): workspace
+// = conv staging, then the conv output (dense NCHW), then the pool counters.
+namespace nt {
+namespace fused {
+inline int64_t align256(int64_t b) { return (b + 255) / 256 * 256; }
+struct Plan {
+  int64_t P, Q, P2, Q2, staging, y_off, y_bytes, ctr_off, ctr_bytes, total;
+};
+inline Plan plan(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k, int64_t r, int64_t s, int64_t pad_h,
+                 int64_t pad_w) {
+  Plan q{};
+  q.P = h + 2 * pad_h - r + 1;
+  q.Q = w + 2 * pad_w - s + 1;
+  q.P2 = q.P > 0 ? (q.P - 1) / 2 + 1 : 0;
+  q.Q2 = q.Q > 0 ? (q.Q - 1) / 2 + 1 : 0;
+  q.staging = align256(nt::tc::conv_workspace_bytes(n, c, h, w, k, r, s, pad_w, 2));
+  q.y_off = q.staging;
+  q.y_bytes = align256(n * k * (q.P > 0 ? q.P : 0) * (q.Q > 0 ? q.Q : 0) * 2);
+  q.ctr_off = q.y_off + q.y_bytes;
+  q.ctr_bytes = n * ((k + 255) / 256) * q.P2 * (int64_t)sizeof(int);
+  q.total = q.ctr_off + q.ctr_bytes;
+  return q;
+}
+}  // namespace fused
+}  // namespace nt
+
+extern "C" int64_t nt_b200_conv2d_max_pool2d_workspace_size(int64_t n, int64_t c, int64_t h, int64_t w, int64_t k,
+                                                            int64_t r, int64_t s, int64_t pad_h, int64_t pad_w,
+                                                            int dtype) {
+  if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0 || pad_h < 0 || pad_w < 0) return 0;
+  if (!nt::is_half_dtype(dtype)) return 0;
+  return nt::fused::plan(n, c, h, w, k, r, s, pad_h, pad_w).total;
+}
+
+extern "C" int nt_b200_conv2d_max_pool2d(const void *input, const void *filter, void *output, int64_t n, int64_t c,
+                                         int64_t h, int64_t w, int64_t k, int64_t r, int64_t s, int64_t pad_h,
+                                         int64_t pad_w, const int64_t *input_strides, const int64_t *filter_strides,
+                                         const int64_t *output_strides, void *workspace, int64_t workspace_bytes,
+                                         int pool_in_conv_kernel, int dtype, void *stream) {
+  if (n < 0 || c < 0 || h < 0 || w < 0 || k < 0 || r <= 0 || s <= 0 || pad_h < 0 || pad_w < 0 ||
+      (pool_in_conv_kernel != 0 && pool_in_conv_kernel != 1))
+    return NT_B200_ERR_INVALID_ARGUMENT;
+  if (!nt::is_half_dtype(dtype)) return NT_B200_ERR_UNSUPPORTED_DTYPE;
+  const nt::fused::Plan q = nt::fused::plan(n, c, h, w, k, r, s, pad_h, pad_w);
+  if (q.P <= 0 || q.Q <= 0) return NT_B200_ERR_SHAPE_MISMATCH;
+  if (n == 0 || k == 0) return 0;
+  if (!input || !filter || !output || !input_strides || !filter_strides || !output_strides || !workspace ||
+      workspace_bytes < q.total || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return NT_B200_ERR_INVALID_ARGUMENT;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  void *y = ws + q.y_off;
+  const int64_t ys[4] = {k * q.P * q.Q, q.P * q.Q, q.Q, 1};
+  const int64_t *is = input_strides, *fs = filter_strides, *os = output_strides;
+  const int rc = !pool_in_conv_kernel ? nt::tc::kNotEligible : NT_DISPATCH_FLOAT(dtype, [&] {
+    using T = scalar_t;
+    const nt::tc::ConvProblem prob{input, filter, y, n, c, h, w, k, r, s, pad_h, pad_w, q.P, q.Q,
+                                   {is[0], is[1], is[2], is[3]}, {fs[0], fs[1], fs[2], fs[3]},
+                                   {ys[0], ys[1], ys[2], ys[3]}};
+    const nt::tc::PoolFusion pool{output, {os[0], os[1], os[2], os[3]}, (int)q.P2, (int)q.Q2,
+                                  reinterpret_cast<int *>(ws + q.ctr_off)};
+    return nt::tc::try_conv<T>(prob, workspace, q.staging, st, &pool);
+  });
+  if (rc != nt::tc::kNotEligible) return rc;
+  // the two kernels: conv2d into the workspace, then max_pool2d (also where
+  // the pool does not fit the conv kernel: small images, a narrow row, a
+  // layout the tensor-core path does not take)
+  const int rc_conv = nt_b200_conv2d(input, filter, y, n, c, h, w, k, r, s, pad_h, pad_w, input_strides,
+                                     filter_strides, ys, q.staging > 0 ? workspace : nullptr, q.staging, dtype, stream);
+  if (rc_conv != 0) return rc_conv;
+  return nt_b200_max_pool2d(y, output, n, k, q.P, q.Q, ys, q.P2, q.Q2, output_strides, 3, 3, 2, 2, 1, 1, dtype,
+                            stream);
+}
+
 extern "C" int nt_b200_attention(const void *q, const void *k, const void *v, int is_causal, void *o,
                                  int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_kv, int64_t head_dim,
                                  const int64_t *q_strides, const int64_t *k_strides, const int64_t *v_strides,

@@ -26,7 +26,10 @@ namespace tc {
 
 constexpr int kNotEligible = -1;
 
-enum class Epilogue { kMatmul, kAddmm, kConv };
+// kConvPool: conv2d whose output also feeds a fused 3x3 / stride 2 / padding 1
+// max pool (CTA-pair kernel only).
+enum class Epilogue { kMatmul, kAddmm, kConv, kConvPool };
+__host__ __device__ constexpr bool is_conv(Epilogue e) { return e == Epilogue::kConv || e == Epilogue::kConvPool; }
 
 struct GemmProblem {
   const void *a, *b, *bias;
@@ -34,6 +37,16 @@ struct GemmProblem {
   int64_t M, N, K;
   int64_t sam, sak, sbk, sbn, sim, sin, som, son;
   float beta, alpha;
+};
+
+// Output side of conv2d + max_pool2d (3x3, stride 2, padding 1) fused in the
+// CTA-pair conv epilogue: pooled output, its strides, extents and the
+// per-(image, channel tile, pool row) counters (workspace, zeroed per call).
+struct PoolFusion {
+  void *out;
+  int64_t os[4];
+  int P2, Q2;
+  int *counters;
 };
 
 struct ConvProblem {
@@ -107,6 +120,13 @@ struct Params {
   // kb = (r, s, channel block cb).
   int conv_c_blocks, conv_s, conv_pad_h, conv_wp, conv_tiles_img, conv_P, conv_Q;
   int64_t conv_osn, conv_osk, conv_osp, conv_osq;
+  // fused max pool (EPI == kConvPool): the conv output above is the pool's
+  // input (a dense NCHW workspace); pool rows of P2 x Q2, and one counter per
+  // (image, output-channel tile, pool row)
+  void *pool_out;
+  int64_t pool_osn, pool_osk, pool_osi, pool_osj;
+  int pool_P, pool_Q;
+  int *pool_counters;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int &mb, int &nb) {
@@ -152,7 +172,7 @@ __device__ __forceinline__ void store_accumulator(const Params &prm, uint32_t tm
   const int row_in_tile = quarter * 32 + lane;
   const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + col0;
   TO *out = static_cast<TO *>(prm.out);
-  if constexpr (EPI == Epilogue::kConv) {
+  if constexpr (is_conv(EPI)) {
     // TMEM lane = position p * Wp + q; columns = output channels.
     const int pos = (int)row0 + row_in_tile;
     const int p = pos / prm.conv_wp, q = pos % prm.conv_wp;
@@ -273,7 +293,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           const uint32_t fb = full_bar(stage);
           ptx::mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
           const int k0 = kb * kblock<TI>();
-          if constexpr (EPI == Epilogue::kConv) {
+          if constexpr (is_conv(EPI)) {
             // A: 128 consecutive rows x 64 channels of the W-padded NHWC input
             // of one image, shifted by filter tap (r, s): position pos reads
             // row pos + (r - pad_h) * Wp + s.  Rows above or below the image
@@ -351,7 +371,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       ptx::tc_fence_after();
       int mb, nb;
       tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
-      if constexpr (EPI == Epilogue::kConv)
+      if constexpr (is_conv(EPI))
         store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
                                        (int64_t)(mb % prm.conv_tiles_img) * BM, (int64_t)nb * BN,
                                        mb / prm.conv_tiles_img);
@@ -394,15 +414,191 @@ constexpr int A_STAGE_BYTES = BM * 128;      // 16 KB
 constexpr int B_STAGE_BYTES = BN_CTA * 128;  // 16 KB
 constexpr int THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + 256 /*barriers*/;
+// kConvPool adds POOL_WARPS pool warps (warps 6..) fed by a ring of RING work
+// cells in shared memory; the control block holds the barriers, the ring's
+// counters (from byte 152) and the cells (from byte 256).
+constexpr int POOL_WARPS = 6;
+constexpr int RING = 128;
+constexpr int CTRL_BYTES = 256 + 8 * RING;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + CTRL_BYTES;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+static_assert(8 * (2 * STAGES + 4) + 8 + 12 <= 256, "control block");
+__host__ __device__ constexpr int threads_for(Epilogue e) {
+  return e == Epilogue::kConvPool ? THREADS + 32 * POOL_WARPS : THREADS;
+}
 
 using gemm::Params;
 using gemm::kblock;
 using gemm::mma_k;
 
+// Fused 3x3 / stride 2 / padding 1 max pool (EPI == kConvPool).
+//
+// Pool row i of image `img` and channel tile nb (256 channels) reads conv rows
+// 2i - 1 .. 2i + 1; the 32-position blocks that cover them are stored by
+// different epilogue warps, CTAs and tiles.  After storing its block, an
+// epilogue warp counts it on every pool row it overlaps (one counter per
+// image, channel tile and pool row, in global memory); the block whose count
+// completes a row hands the row, as one work cell per 32 channels, to the pool
+// warps of its own CTA through a ring in shared memory.  No warp waits for
+// another CTA, and the epilogue only waits when the ring is full.  The conv
+// output is read back with L1-bypassing loads: L1 is not coherent with the
+// other SMs' stores.
+//
+// The ring is a bounded multi-producer multi-consumer queue of RING cells
+// (sequence number, work code): the producer of position t waits for cell
+// t % RING to carry sequence t, writes the code and publishes t + 1; the
+// consumer of t waits for t + 1, reads the code and frees the cell with
+// t + RING.  Positions are handed out by atomics on `tail` (producers) and
+// `head` (consumers).  A work code is 8 * (pool-row counter index) + part.
+struct PoolRing {
+  int *tail, *head, *epi_done;
+  int *cells;  // RING x {sequence, code}
+};
+
+__device__ __forceinline__ int ld_volatile_shared(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
+// Epilogue side: count the warp's block [wpos, wpos + 32) of image `img` and
+// push the pool rows it completes.  Lane 0 only.
+__device__ __forceinline__ void pool_count_and_push(const Params &prm, const PoolRing &ring, int img, int wpos,
+                                                    int nb, volatile int *abort_flag) {
+  const int Wp = prm.conv_wp, P = prm.conv_P, P2 = prm.pool_P;
+  const int lo = wpos, hi = min(wpos + 32, P * Wp);
+  if (lo >= hi) return;
+  __threadfence();  // the warp's stores of this block are visible device-wide before they are counted
+  const int p_lo = lo / Wp, p_hi = (hi - 1) / Wp;
+  const int i_first = max(0, p_lo / 2 - 1), i_last = min(P2 - 1, (p_hi + 1) / 2);
+  const int64_t row0 = ((int64_t)img * prm.tiles_n + nb) * P2;
+  const int64_t left = (prm.N - (int64_t)nb * 256 + 31) / 32;
+  const int parts = left < 8 ? (int)left : 8;
+  for (int i = i_first; i <= i_last; ++i) {
+    const int r_lo = max(0, 2 * i - 1), r_hi = min(P - 1, 2 * i + 1);
+    if (r_hi < p_lo || r_lo > p_hi) continue;
+    const int b_lo = r_lo * Wp, b_hi = (r_hi + 1) * Wp;    // the pool row's input positions
+    const int required = (b_hi - 1) / 32 - b_lo / 32 + 1;  // 32-position blocks covering them
+    if (atomicAdd(prm.pool_counters + row0 + i, 1) != required - 1) continue;
+    __threadfence();  // the other blocks' stores are visible to this CTA's pool warps from here on
+    const int pos0 = atomicAdd(ring.tail, parts);
+    for (int j = 0; j < parts; ++j) {
+      const int pos = pos0 + j;
+      int *cell = ring.cells + 2 * (pos % RING);
+      const uint64_t t0 = ptx::global_timer_ns();
+      bool ok = true;
+      for (uint32_t it = 0; ld_volatile_shared(cell) != pos; ++it) {
+        if (*abort_flag) { ok = false; break; }
+        if ((it & 15u) == 15u && ptx::global_timer_ns() - t0 > ptx::kWaitLimitNs) {
+          *abort_flag = 1;
+          record_error(NT_B200_ERR_DEVICE_TIMEOUT);
+          ok = false;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (!ok) return;
+      cell[1] = (int)((row0 + i) * 8 + j);
+      __threadfence_block();
+      *reinterpret_cast<volatile int *>(cell) = pos + 1;
+    }
+  }
+}
+
+// One work cell: pool row i, channels [256 nb + 32 part, + 32) of image img.
+// 8 lanes per channel (lane v holds conv columns [8v, 8v + 8) of the three
+// input rows and takes column 8v - 1 from lane v - 1), 4 channels per pass,
+// all 8 passes' loads in flight at once; lane v writes pool columns
+// [4v, 4v + 4) with one 8-byte store.  The host only fuses when Q % 8 == 0,
+// Q <= 64 and the pooled rows take 8-byte stores.
+template <typename TO>
+__device__ __forceinline__ void pool_part(const Params &prm, int img, int nb, int i, int part, int lane) {
+  const int P = prm.conv_P, Q = prm.conv_Q;
+  const int v = lane & 7, g = lane >> 3;
+  const bool col_ok = v < Q / 8;
+  const TO ninf = from_f<TO>(-INFINITY);
+  const unsigned short ninf_bits = *reinterpret_cast<const unsigned short *>(&ninf);
+  const uint32_t ninf2 = (uint32_t)ninf_bits | ((uint32_t)ninf_bits << 16);
+  const TO *ybase = static_cast<const TO *>(prm.out) + (int64_t)img * prm.conv_osn;
+  TO *zbase = static_cast<TO *>(prm.pool_out) + (int64_t)img * prm.pool_osn;
+  const int64_t k0 = (int64_t)nb * 256 + part * 32;
+  int4 raw[8][3];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int64_t k = k0 + 4 * u + g;
+#pragma unroll
+    for (int rr = 0; rr < 3; ++rr) {
+      const int r = 2 * i - 1 + rr;
+      raw[u][rr] = make_int4((int)ninf2, (int)ninf2, (int)ninf2, (int)ninf2);
+      if (col_ok && k < prm.N && r >= 0 && r < P)
+        raw[u][rr] = __ldcg(reinterpret_cast<const int4 *>(ybase + k * prm.conv_osk + (int64_t)r * prm.conv_osp) + v);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int64_t k = k0 + 4 * u + g;
+    TO vm[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const TO *r0 = reinterpret_cast<const TO *>(&raw[u][0]);
+      const TO *r1 = reinterpret_cast<const TO *>(&raw[u][1]);
+      const TO *r2 = reinterpret_cast<const TO *>(&raw[u][2]);
+      vm[e] = __hmax(__hmax(r0[e], r1[e]), r2[e]);
+    }
+    // conv column 8v - 1 is lane v - 1's last element (padding for v = 0)
+    const unsigned short last = *reinterpret_cast<const unsigned short *>(&vm[7]);
+    const unsigned short prev = (unsigned short)__shfl_up_sync(0xffffffffu, (unsigned)last, 1, 8);
+    TO left;
+    *reinterpret_cast<unsigned short *>(&left) = prev;
+    if (v == 0) left = ninf;
+    alignas(8) TO o[4];
+#pragma unroll
+    for (int oo = 0; oo < 4; ++oo) o[oo] = __hmax(__hmax(oo == 0 ? left : vm[2 * oo - 1], vm[2 * oo]), vm[2 * oo + 1]);
+    if (col_ok && k < prm.N)
+      *reinterpret_cast<uint2 *>(zbase + k * prm.pool_osk + (int64_t)i * prm.pool_osi + 4 * v) =
+          *reinterpret_cast<const uint2 *>(o);
+  }
+}
+
+// Pool warp: takes ring positions one at a time until the CTA's 4 epilogue
+// warps have finished and every pushed position is taken.  Waits are bounded.
+template <typename TO>
+__device__ __forceinline__ void pool_worker(const Params &prm, const PoolRing &ring, int lane,
+                                            volatile int *abort_flag) {
+  for (;;) {
+    int code = -1;
+    if (lane == 0) {
+      const uint64_t t0 = ptx::global_timer_ns();
+      const int pos = atomicAdd(ring.head, 1);
+      int *cell = ring.cells + 2 * (pos % RING);
+      for (uint32_t it = 0;; ++it) {
+        if (ld_volatile_shared(cell) == pos + 1) {
+          __threadfence_block();
+          code = ld_volatile_shared(cell + 1);
+          __threadfence_block();
+          *reinterpret_cast<volatile int *>(cell) = pos + RING;
+          break;
+        }
+        if (ld_volatile_shared(ring.epi_done) == 4) {
+          __threadfence_block();
+          if (ld_volatile_shared(ring.tail) <= pos) break;  // nothing more will be pushed here
+        }
+        if (*abort_flag) break;
+        if ((it & 15u) == 15u && ptx::global_timer_ns() - t0 > ptx::kWaitLimitNs) {
+          *abort_flag = 1;
+          record_error(NT_B200_ERR_DEVICE_TIMEOUT);
+          break;
+        }
+        __nanosleep(128);
+      }
+      if (code >= 0) __threadfence();  // pairs with the producer's device-wide fence
+    }
+    code = __shfl_sync(0xffffffffu, code, 0);
+    if (code < 0) return;
+    const int part = code & 7, row = code >> 3;
+    const int i = row % prm.pool_P, t = row / prm.pool_P;
+    pool_part<TO>(prm, t / prm.tiles_n, t % prm.tiles_n, i, part, lane);
+  }
+}
+
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(EPI), 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  Params prm) {
   extern __shared__ uint8_t smem_raw[];
@@ -421,6 +617,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   auto tempty_bar = [&](int b) { return ctrl_addr + 8u * (2 * STAGES + 2 + b); };
   volatile uint32_t *tmem_base_ptr = reinterpret_cast<volatile uint32_t *>(ctrl + 8 * (2 * STAGES + 4));
   volatile int *abort_flag = reinterpret_cast<volatile int *>(ctrl + 8 * (2 * STAGES + 4) + 4);
+  int *ring_words = reinterpret_cast<int *>(ctrl + 8 * (2 * STAGES + 4) + 8);
+  const PoolRing ring{ring_words, ring_words + 1, ring_words + 2, reinterpret_cast<int *>(ctrl + 256)};
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = ptx::cluster_ctarank();
@@ -434,6 +632,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       ptx::mbar_init(tempty_bar(b), 8);  // one arrival per epilogue warp of both CTAs
     }
     *abort_flag = 0;
+    if constexpr (EPI == Epilogue::kConvPool) {
+      *ring.tail = *ring.head = *ring.epi_done = 0;
+      for (int c = 0; c < RING; ++c) ring.cells[2 * c] = c;
+    }
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tmap_a);
     ptx::prefetch_tmap(&tmap_b);
@@ -468,7 +670,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           const uint32_t fb = ptx::mapa(full_bar(stage), 0);
           const uint32_t a_dst = a_base + stage * A_STAGE_BYTES, b_dst = b_base + stage * B_STAGE_BYTES;
           const int k0 = kb * kblock<TI>();
-          if constexpr (EPI == Epilogue::kConv) {
+          if constexpr (is_conv(EPI)) {
             const int cb = kb % prm.conv_c_blocks, rs = kb / prm.conv_c_blocks;
             const int r = rs / prm.conv_s, sx = rs % prm.conv_s;
             const int img = mb / prm.conv_tiles_img;
@@ -534,7 +736,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         if (ok) ptx::mma_commit_pair_both(tfull_bar(buf));
       }
     }
-  } else {
+  } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     int local = 0;
@@ -545,7 +747,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       ptx::tc_fence_after();
       int mb, nb;
       gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
-      if constexpr (EPI == Epilogue::kConv)
+      if constexpr (is_conv(EPI))
         gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
                                              (int64_t)(mb % prm.conv_tiles_img) * (2 * BM) + rank * BM,
                                              (int64_t)nb * BN, mb / prm.conv_tiles_img);
@@ -555,7 +757,21 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(buf), 0));
+      if constexpr (EPI == Epilogue::kConvPool)
+        if (lane == 0)
+          pool_count_and_push(prm, ring, mb / prm.conv_tiles_img,
+                              (mb % prm.conv_tiles_img) * (2 * BM) + (int)rank * BM + quarter * 32, nb, abort_flag);
     }
+    if constexpr (EPI == Epilogue::kConvPool) {
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();  // this warp's pushes are published before it counts as done
+        atomicAdd(ring.epi_done, 1);
+      }
+    }
+  } else if constexpr (EPI == Epilogue::kConvPool) {
+    // ---------------------------------------------------------------- pool warps (both CTAs)
+    pool_worker<TO>(prm, ring, lane, abort_flag);
   }
 
   __syncwarp();
@@ -574,6 +790,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
 int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params &prm, cudaStream_t stream) {
   auto kern = gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>;
+  constexpr int threads = gemm2::threads_for(EPI);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM_BYTES);
   if (e != cudaSuccess) return (int)e;
   static int resident_pairs[64] = {};  // per device, filled on first use
@@ -583,7 +800,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
   if (pairs == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
-    cfg.blockDim = dim3(gemm2::THREADS, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = gemm2::SMEM_BYTES;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
@@ -600,7 +817,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
   }
   const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
   const int grid_pairs = (int)(tiles < pairs ? tiles : pairs);
-  kern<<<2 * grid_pairs, gemm2::THREADS, gemm2::SMEM_BYTES, stream>>>(ta, tb, prm);
+  kern<<<2 * grid_pairs, threads, gemm2::SMEM_BYTES, stream>>>(ta, tb, prm);
   return launch_status();
 }
 
@@ -808,7 +1025,8 @@ inline int64_t conv_workspace_bytes(int64_t n, int64_t c, int64_t h, int64_t w, 
 }
 
 template <typename T>
-int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cudaStream_t stream) {
+int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cudaStream_t stream,
+             const PoolFusion *pool = nullptr) {
   if constexpr (sizeof(T) != 2) {
     return kNotEligible;
   } else {
@@ -817,6 +1035,13 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     if (need == 0 || workspace == nullptr || workspace_bytes < need) return kNotEligible;
     if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return kNotEligible;
     const int64_t wp = p.w + 2 * p.pad_w;
+    // the fused pool runs in the CTA-pair kernel, one 32-position block per
+    // epilogue warp spanning at most two conv rows; its work codes
+    // (8 per pool row of a channel tile) must fit an int
+    if (pool && (p.P * wp <= BM || wp < 32 || p.Q % 8 != 0 || p.Q > 64 || pool->os[3] != 1 || pool->os[0] % 4 != 0 ||
+                 pool->os[1] % 4 != 0 || pool->os[2] % 4 != 0 || (reinterpret_cast<uintptr_t>(pool->out) & 7u) != 0 ||
+                 p.n * ((p.k + BN - 1) / BN) * pool->P2 * 8 >= (1LL << 31)))
+      return kNotEligible;
     if (p.h == 0 || p.w == 0 || p.n >= 65535 || p.c > (1 << 20) || p.h > (1 << 20) || wp > (1 << 20) ||
         p.k > (1 << 20) || p.r * p.s * p.c > (1 << 30) || p.pad_h > (1 << 20) ||
         (p.h + 2 * p.pad_h + p.r) * wp > (1LL << 30))
@@ -892,6 +1117,20 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     prm.K = p.r * p.s * p.c;
     const int64_t tiles = tiles_m * prm.tiles_n;
     if (tiles > (1LL << 30)) return kNotEligible;
+    if (pool) {
+      prm.pool_out = pool->out;
+      prm.pool_osn = pool->os[0];
+      prm.pool_osk = pool->os[1];
+      prm.pool_osi = pool->os[2];
+      prm.pool_osj = pool->os[3];
+      prm.pool_P = pool->P2;
+      prm.pool_Q = pool->Q2;
+      prm.pool_counters = pool->counters;
+      const cudaError_t e = cudaMemsetAsync(pool->counters, 0, (size_t)p.n * prm.tiles_n * pool->P2 * sizeof(int),
+                                            stream);
+      if (e != cudaSuccess) return (int)e;
+      return launch_pair<T, T, Epilogue::kConvPool, false>(ta, tb, prm, stream);
+    }
     if (pair) return launch_pair<T, T, Epilogue::kConv, false>(ta, tb, prm, stream);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     auto kern = gemm_kernel<T, T, Epilogue::kConv, false>;

@@ -181,6 +181,41 @@ def conv2d(input, filter, padding=0):
     return conv2d_kernel(input, filter, output, padding_h=padding_h, padding_w=padding_w)
 
 
+def conv2d_max_pool2d(input, filter, padding=0, pool_in_conv_kernel=False):
+    """max_pool2d(conv2d(input, filter, padding), 3x3 window, stride 2,
+    padding 1) in one call, bit-identical to the two programs in sequence.
+    By default the conv kernel and then the max_pool2d kernel run (the faster
+    order on B200); `pool_in_conv_kernel=True` pools inside the tensor-core
+    conv kernel where the shape allows."""
+    if isinstance(padding, int):
+        padding = (padding, padding)
+    ph, pw = int(padding[0]), int(padding[1])
+    if input.dim() != 4 or filter.dim() != 4 or input.device.type != "cuda":
+        raise TypeError("conv2d_max_pool2d takes 4-D CUDA tensors.")
+    if input.dtype != filter.dtype or input.dtype not in HALF_DTYPES:
+        raise TypeError("conv2d_max_pool2d takes float16 or bfloat16 input and filter of one dtype.")
+    n, c, h, wd = input.shape
+    k, c2, r, s = filter.shape
+    if c2 != c:
+        raise TypeError("conv2d_max_pool2d channel extents disagree.")
+    p, q = h + 2 * ph - r + 1, wd + 2 * pw - s + 1
+    out = torch.empty((n, k, (p - 1) // 2 + 1, (q - 1) // 2 + 1), device=input.device, dtype=input.dtype)
+    if out.numel() == 0:
+        return out
+    code = dtype_code(input.dtype)
+    nbytes = _lib_call("nt_b200_conv2d_max_pool2d_workspace_size", n, c, h, wd, k, r, s, ph, pw, code)
+    workspace = torch.empty(nbytes, dtype=torch.uint8, device=input.device)
+    xs, ws, os_ = (_lib.int64_array(t.stride()) for t in (input, filter, out))
+    with torch.cuda.device(input.device):
+        stream = torch.cuda.current_stream(input.device).cuda_stream
+        code_rc = _lib_call("nt_b200_conv2d_max_pool2d", ptr(input), ptr(filter), ptr(out), n, c, h, wd, k, r, s,
+                            ph, pw, xs, ws, os_, ptr(workspace), nbytes, int(bool(pool_in_conv_kernel)), code,
+                            stream)
+    if code_rc != 0:
+        raise KernelLaunchError(code_rc)
+    return out
+
+
 # --------------------------------------------------------------------- max_pool2d
 def _make_max_pool2d_launch(ceil_mode):
     del ceil_mode  # output extents come from the output tensor
@@ -530,6 +565,7 @@ __all__ = [
     "attention_kernel",
     "conv2d",
     "conv2d_kernel",
+    "conv2d_max_pool2d",
     "dropout",
     "dropout_kernel",
     "matmul",

@@ -3,7 +3,7 @@
 Runs the reference's own operator programs (PPPoint-t/ninetoothed 0.26.0, the
 arrangements/applications of its tests/test_*.py) on the CPU under the Triton
 interpreter and stores inputs and outputs as .npz fixtures.  This script needs
-the reference source tree (set NINETOOTHED_REFERENCE, default /root/reference)
+the reference source tree (point NINETOOTHED_REFERENCE at it)
 and is run by hand in a container that has it; tests only read the .npz files.
 
 Harness settings (none of them edits the reference):
@@ -24,7 +24,9 @@ from pathlib import Path
 
 import numpy as np
 
-REFERENCE = Path(os.environ.get("NINETOOTHED_REFERENCE", "/root/reference"))
+if "NINETOOTHED_REFERENCE" not in os.environ:
+    sys.exit("set NINETOOTHED_REFERENCE to the reference source tree (with src/ and tests/)")
+REFERENCE = Path(os.environ["NINETOOTHED_REFERENCE"])
 OUT = Path(__file__).resolve().parent
 
 os.environ["TRITON_INTERPRET"] = "1"

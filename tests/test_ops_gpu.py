@@ -437,3 +437,28 @@ def test_softmax_host_streaming_matches_device_softmax(rows, cols, chunks):
     again = programs.softmax_host(x, out, chunks=chunks)  # reuse of the output buffer
     torch.cuda.current_stream().synchronize()
     assert again is out and torch.equal(out, expected)
+
+
+@pytest.mark.parametrize("inside", [False, True], ids=["two_kernels", "pool_in_conv_kernel"])
+@pytest.mark.parametrize(
+    "nchw, k, rs, pad, dtype",
+    [
+        ((4, 64, 56, 56), 256, (3, 3), (1, 1), torch.float16),   # pool fits the conv kernel (BASELINE shape, N=4)
+        ((2, 72, 45, 48), 320, (3, 3), (1, 1), torch.bfloat16),  # fits: odd height, two channel tiles
+        ((3, 32, 36, 64), 64, (5, 5), (2, 2), torch.float16),    # fits: 5x5 taps, 64 columns
+        ((2, 72, 45, 45), 320, (3, 3), (1, 1), torch.bfloat16),  # odd width: conv + pool launches
+        ((3, 32, 40, 33), 64, (5, 5), (2, 2), torch.float16),    # odd width, 5x5: conv + pool launches
+        ((2, 16, 12, 12), 32, (3, 3), (1, 1), torch.float16),    # narrow rows: conv + pool launches
+        ((1, 12, 20, 20), 16, (3, 3), (0, 0), torch.float16),    # C % 8 != 0: CUDA-core conv + pool
+    ],
+)
+def test_conv2d_max_pool2d_equals_the_two_programs(nchw, k, rs, pad, dtype, inside):
+    gen = torch.Generator().manual_seed(sum(nchw) + k + rs[0])
+    x = torch.randn(nchw, generator=gen).to(dtype).to(DEV)
+    w = (torch.randn((k, nchw[1]) + rs, generator=gen) * 0.1).to(dtype).to(DEV)
+    fused = programs.conv2d_max_pool2d(x, w, padding=pad, pool_in_conv_kernel=inside)
+    two = programs.max_pool2d(programs.conv2d(x, w, padding=pad), (3, 3), stride=2, padding=1)
+    assert fused.shape == two.shape
+    assert torch.equal(fused, two)  # bit-identical
+    again = programs.conv2d_max_pool2d(x, w, padding=pad, pool_in_conv_kernel=inside)  # counters restart per call
+    assert torch.equal(again, two)
