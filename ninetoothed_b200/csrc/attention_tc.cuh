@@ -525,12 +525,12 @@ int try_attention(const AttentionProblem &p, cudaStream_t stream) {
     const int64_t grid = items < sm_count() ? items : sm_count();  // persistent: one CTA per SM
     if (p.D <= 64) {
       auto kern = attention_kernel<T, 64>;
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<64>::SMEM_BYTES);
+      cudaError_t e = smem_optin<attention_kernel<T, 64>>(Layout<64>::SMEM_BYTES);
       if (e != cudaSuccess) return (int)e;
       kern<<<(unsigned)grid, THREADS, Layout<64>::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
     } else {
       auto kern = attention_kernel<T, 128>;
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<128>::SMEM_BYTES);
+      cudaError_t e = smem_optin<attention_kernel<T, 128>>(Layout<128>::SMEM_BYTES);
       if (e != cudaSuccess) return (int)e;
       kern<<<(unsigned)grid, THREADS, Layout<128>::SMEM_BYTES, stream>>>(tq, tk, tv, prm);
     }

@@ -8,9 +8,28 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/nt_b200.h"
 
 namespace nt {
+
+// Opts kernel `Kern` in to `bytes` of dynamic shared memory once per device:
+// the first launch on a device sets the attribute, later launches read one
+// atomic word.  No lock on the launch path; two host threads that race on a
+// device's first launch both set the (idempotent) attribute.
+template <auto Kern>
+inline cudaError_t smem_optin(int bytes) {
+  static std::atomic<uint64_t> done{0};  // bit d: device d has the attribute
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
+  e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
 
 // Device error word of this library (one per device, zero-initialised at load).
 // The library is a single translation unit, so this is its only definition.

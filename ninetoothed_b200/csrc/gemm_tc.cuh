@@ -791,12 +791,12 @@ template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
 int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params &prm, cudaStream_t stream) {
   auto kern = gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>;
   constexpr int threads = gemm2::threads_for(EPI);
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm2::SMEM_BYTES);
+  cudaError_t e = smem_optin<gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>>(gemm2::SMEM_BYTES);
   if (e != cudaSuccess) return (int)e;
-  static int resident_pairs[64] = {};  // per device, filled on first use
+  static std::atomic<int> resident_pairs[64] = {};  // per device, filled on first use (any thread)
   int device = 0;
   cudaGetDevice(&device);
-  int pairs = device < 64 ? resident_pairs[device] : 0;
+  int pairs = (device >= 0 && device < 64) ? resident_pairs[device].load(std::memory_order_relaxed) : 0;
   if (pairs == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
@@ -813,7 +813,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
       cudaGetLastError();
       pairs = sm_count() / 2;
     }
-    if (device < 64) resident_pairs[device] = pairs;
+    if (device >= 0 && device < 64) resident_pairs[device].store(pairs, std::memory_order_relaxed);
   }
   const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
   const int grid_pairs = (int)(tiles < pairs ? tiles : pairs);
@@ -873,7 +873,8 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
                   : launch_pair<TI, TO, EPI, false>(ta, tb, prm, stream);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     auto kern = b_mn ? gemm_kernel<TI, TO, EPI, true> : gemm_kernel<TI, TO, EPI, false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = b_mn ? smem_optin<gemm_kernel<TI, TO, EPI, true>>(SMEM_BYTES)
+                         : smem_optin<gemm_kernel<TI, TO, EPI, false>>(SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, prm);
     return launch_status();
@@ -1134,7 +1135,7 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     if (pair) return launch_pair<T, T, Epilogue::kConv, false>(ta, tb, prm, stream);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     auto kern = gemm_kernel<T, T, Epilogue::kConv, false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = smem_optin<gemm_kernel<T, T, Epilogue::kConv, false>>(SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, prm);
     return launch_status();
