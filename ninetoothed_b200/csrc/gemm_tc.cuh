@@ -64,6 +64,13 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
 
 EncodeTiledFn encode_tiled_fn();
 
+using EncodeIm2colFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const int *, const int *, cuuint32_t, cuuint32_t,
+                                    const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeIm2colFn encode_im2col_fn();
+
 // 2-D tensor map over a matrix with a contiguous inner dimension.
 inline bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                          uint64_t outer, uint64_t outer_stride_elems, uint32_t box_inner, uint32_t box_outer) {
@@ -120,6 +127,11 @@ struct Params {
   // kb = (r, s, channel block cb).
   int conv_c_blocks, conv_s, conv_pad_h, conv_wp, conv_tiles_img, conv_P, conv_Q;
   int64_t conv_osn, conv_osk, conv_osp, conv_osq;
+  // conv_flat (CTA-pair kConv only): m-blocks tile the batch's output pixels
+  // as one range f = image * conv_pwp + p * Q + q (conv_pwp = P * Q, conv_wp
+  // = Q: no padding columns), and A is loaded by im2col-mode TMA from the
+  // unpadded NHWC input; conv_n images
+  int conv_flat, conv_pwp, conv_n, conv_pad_w;
   // fused max pool (EPI == kConvPool): the conv output above is the pool's
   // input (a dense NCHW workspace); pool rows of P2 x Q2, and one counter per
   // (image, output-channel tile, pool row)
@@ -174,9 +186,14 @@ __device__ __forceinline__ void store_accumulator(const Params &prm, uint32_t tm
   TO *out = static_cast<TO *>(prm.out);
   if constexpr (is_conv(EPI)) {
     // TMEM lane = position p * Wp + q; columns = output channels.
-    const int pos = (int)row0 + row_in_tile;
+    int pos = (int)row0 + row_in_tile;
+    if (prm.conv_flat) {  // row0 is a flat position (< 2^31): split it into image and position
+      const int f = (int)row0 + row_in_tile;
+      img = f / prm.conv_pwp;
+      pos = f - img * prm.conv_pwp;
+    }
     const int p = pos / prm.conv_wp, q = pos % prm.conv_wp;
-    const bool pix_ok = p < prm.conv_P && q < prm.conv_Q;
+    const bool pix_ok = img < prm.conv_n && p < prm.conv_P && q < prm.conv_Q;
     TO *pix = out + (int64_t)img * prm.conv_osn + (int64_t)p * prm.conv_osp + (int64_t)q * prm.conv_osq;
 #pragma unroll 1
     for (int c = 0; c < 256 / 32; ++c) {
@@ -664,6 +681,23 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
         const int m0 = mb * (2 * BM) + (int)rank * BM;   // this CTA's rows of A
         const int n0 = nb * BN + (int)rank * BN_CTA;     // this CTA's half of B
+        // conv: image and first position of this CTA's rows; flat tiling
+        // splits the first output pixel into (image, p, q) once per tile
+        int img_a = 0, pos_a = 0, p_a = 0, q_a = 0;
+        if constexpr (is_conv(EPI)) {
+          img_a = mb / prm.conv_tiles_img;
+          pos_a = (mb % prm.conv_tiles_img) * (2 * BM) + (int)rank * BM;
+          if constexpr (EPI == Epilogue::kConv) {
+            if (prm.conv_flat) {
+              int f0 = mb * (2 * BM) + (int)rank * BM;  // < 2^31: checked on the host
+              if (f0 >= prm.conv_n * prm.conv_pwp) f0 = 0;  // rows past the batch: any in-range start (discarded)
+              img_a = f0 / prm.conv_pwp;
+              pos_a = f0 - img_a * prm.conv_pwp;
+              p_a = pos_a / prm.conv_wp;
+              q_a = pos_a - p_a * prm.conv_wp;
+            }
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
           if (rank == 0) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * (A_STAGE_BYTES + B_STAGE_BYTES));
@@ -673,10 +707,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if constexpr (is_conv(EPI)) {
             const int cb = kb % prm.conv_c_blocks, rs = kb / prm.conv_c_blocks;
             const int r = rs / prm.conv_s, sx = rs % prm.conv_s;
-            const int img = mb / prm.conv_tiles_img;
-            const int pos0 = (mb % prm.conv_tiles_img) * (2 * BM) + (int)rank * BM;
-            ptx::tma_load_3d_pair(a_dst, &tmap_a, fb, cb * gemm::BK, pos0 + (r - prm.conv_pad_h) * prm.conv_wp + sx,
-                                  img);
+            bool flat = false;
+            if constexpr (EPI == Epilogue::kConv) flat = prm.conv_flat != 0;
+            if (flat)  // 128 output pixels from (img_a, p_a, q_a) on, across rows and images, tap (r, sx)
+              ptx::tma_load_im2col_4d_pair(a_dst, &tmap_a, fb, cb * gemm::BK, q_a - prm.conv_pad_w,
+                                           p_a - prm.conv_pad_h, img_a, (uint16_t)sx, (uint16_t)r);
+            else
+              ptx::tma_load_3d_pair(a_dst, &tmap_a, fb, cb * gemm::BK,
+                                    pos_a + (r - prm.conv_pad_h) * prm.conv_wp + sx, img_a);
             ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, cb * gemm::BK, rs, n0);
           } else {
             ptx::tma_load_2d_pair(a_dst, &tmap_a, fb, k0, m0);
@@ -884,7 +922,9 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
 // ------------------------------------------------------------------ conv2d staging
 // The staged input is NHWC with pad_w zero columns on each side of every row
 // (row width Wp = W + 2 pad_w): pixel (h, w) of image n sits at row
-// (n * H + h) * Wp + w + pad_w of a [n * H * Wp, C] matrix.
+// (n * H + h) * Wp + w + pad_w of a [n * H * Wp, C] matrix.  The im2col-mode
+// path (flat tiling) stages without the padding columns (Wp = W, pad_w = 0):
+// its TMA reads the padding as zeros from outside the tensor.
 
 // Zeroes the pad_w columns on both sides of the staged rows whose first pixel
 // lies in this CTA's pixel range [p0, p0 + 64), for channels [c0, c0 + 64):
@@ -1047,6 +1087,19 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
         p.k > (1 << 20) || p.r * p.s * p.c > (1 << 30) || p.pad_h > (1 << 20) ||
         (p.h + 2 * p.pad_h + p.r) * wp > (1LL << 30))
       return kNotEligible;
+    // CTA pairs (256-position tiles) unless an image has a single 128-position tile
+    const bool pair = p.P * wp > BM;
+    const int tile_m = pair ? 2 * BM : BM;
+    // Flat tiling for the CTA-pair conv without the fused pool: the batch's
+    // N * P * Q output pixels are one range of tiles, whose A rows
+    // im2col-mode TMA walks across rows and images of the unpadded NHWC input
+    // (padding read as zeros from outside the tensor).  The map's box corners
+    // (-pad, pad - (filter - 1)) must lie in [-128, 127]; inputs under 128 KB
+    // keep the padded-row path.
+    const bool flat = pair && !pool && p.pad_h <= 127 && p.pad_w <= 127 && p.r - 1 - p.pad_h <= 128 &&
+                      p.s - 1 - p.pad_w <= 128 && p.r <= 255 && p.s <= 255 && p.n * p.h * p.w * p.c * 2 >= 131072 &&
+                      p.n * p.P * p.Q < (1LL << 31) - 2 * tile_m && encode_im2col_fn() != nullptr;
+    const int64_t wp_stage = flat ? p.w : wp, pad_w_stage = flat ? 0 : p.pad_w;
     T *act = static_cast<T *>(workspace);
     T *flt = reinterpret_cast<T *>(static_cast<uint8_t *>(workspace) + ((p.n * p.h * wp * p.c * 2 + 255) / 256) * 256);
     {
@@ -1059,22 +1112,31 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
                                 p.is[0] % 8 == 0 && (reinterpret_cast<uintptr_t>(p.input) & 15u) == 0;
       if (dense_planes)
         nchw_to_nhwc_vec_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
-                                                             (int)p.w, (int)wp, (int)p.pad_w, p.is[0], p.is[1],
-                                                             filter);
+                                                             (int)p.w, (int)wp_stage, (int)pad_w_stage, p.is[0],
+                                                             p.is[1], filter);
       else
         nchw_to_nhwc_kernel<T><<<grid, 256, 0, stream>>>(static_cast<const T *>(p.input), act, (int)p.c, HW,
-                                                         (int)p.w, (int)wp, (int)p.pad_w, p.is[0], p.is[1],
-                                                         p.is[2], p.is[3], filter);
+                                                         (int)p.w, (int)wp_stage, (int)pad_w_stage, p.is[0],
+                                                         p.is[1], p.is[2], p.is[3], filter);
       const int st = launch_status();
       if (st != 0) return st;
     }
     EncodeTiledFn fn = encode_tiled_fn();
     if (!fn) return kNotEligible;
-    // CTA pairs (256-position tiles) unless an image has a single 128-position tile
-    const bool pair = p.P * wp > BM;
-    const int tile_m = pair ? 2 * BM : BM;
     CUtensorMap ta, tb;
-    {
+    if (flat) {
+      // NHWC dims {C, W, H, N}; the box walks output pixels: corners {W, H}
+      const cuuint64_t dims[4] = {(cuuint64_t)p.c, (cuuint64_t)p.w, (cuuint64_t)p.h, (cuuint64_t)p.n};
+      const cuuint64_t strides[3] = {(cuuint64_t)(p.c * 2), (cuuint64_t)(p.w * p.c * 2),
+                                     (cuuint64_t)(p.h * p.w * p.c * 2)};
+      const int lower[2] = {-(int)p.pad_w, -(int)p.pad_h};
+      const int upper[2] = {(int)(p.pad_w - (p.s - 1)), (int)(p.pad_h - (p.r - 1))};
+      const cuuint32_t estr[4] = {1, 1, 1, 1};
+      if (encode_im2col_fn()(&ta, tmap_dtype<T>(), 4, act, dims, strides, lower, upper, 64, (cuuint32_t)BM, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return kNotEligible;
+    } else {
       // [image][H * Wp rows][C]: one image per outer index, so rows shifted
       // above or below an image read as zero instead of a neighbour's pixels
       const cuuint64_t dims[3] = {(cuuint64_t)p.c, (cuuint64_t)(p.h * wp), (cuuint64_t)p.n};
@@ -1109,7 +1171,15 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
     prm.conv_osk = p.os[1];
     prm.conv_osp = p.os[2];
     prm.conv_osq = p.os[3];
-    const int64_t tiles_m = p.n * prm.conv_tiles_img;
+    prm.conv_n = (int)p.n;
+    prm.conv_pad_w = (int)p.pad_w;
+    if (flat) {
+      prm.conv_flat = 1;
+      prm.conv_wp = (int)p.Q;  // no padding columns
+      prm.conv_pwp = (int)(p.P * p.Q);
+      prm.conv_tiles_img = (int)((p.n * p.P * p.Q + tile_m - 1) / tile_m);  // all tiles in one range
+    }
+    const int64_t tiles_m = flat ? prm.conv_tiles_img : p.n * prm.conv_tiles_img;
     prm.tiles_m = (int)tiles_m;
     prm.tiles_n = (int)((p.k + BN - 1) / BN);
     prm.num_kb = (int)(p.r * p.s * prm.conv_c_blocks);

@@ -37,6 +37,17 @@ EncodeTiledFn encode_tiled_fn() {
   }();
   return fn;
 }
+EncodeIm2colFn encode_im2col_fn() {
+  static EncodeIm2colFn fn = []() -> EncodeIm2colFn {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeIm2colFn>(ptr);
+  }();
+  return fn;
+}
 }  // namespace tc
 
 }  // namespace nt

@@ -132,6 +132,21 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// im2col-mode load of a CTA pair's operand (4-D NHWC tensor map, dims
+// {C, W, H, N}): channelsPerPixel channels from c of pixelsPerColumn pixels
+// walked in (n, h, w) order through the map's bounding box from (w, h, n),
+// each read at (w + off_w, h + off_h); pixels outside the tensor read zero.
+// Completes on the even CTA's barrier `bar` (a cluster address).
+__device__ __forceinline__ void tma_load_im2col_4d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar, int32_t c,
+                                                        int32_t w, int32_t h, int32_t n, uint16_t off_w,
+                                                        uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.im2col.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 // ------------------------------------------------------------------ clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

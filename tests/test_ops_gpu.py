@@ -412,6 +412,15 @@ def test_conv2d_baseline_config_sampled_images():
         ((2, 72, 12, 12), 320, (3, 3), (1, 1), torch.bfloat16),  # 168 positions: one pair tile, 2 N tiles, C % 64
         ((2, 64, 20, 23), 64, (5, 5), (2, 2), torch.float16),    # 5x5 taps, odd width
         ((1, 8, 40, 40), 16, (1, 1), (0, 0), torch.float16),     # 1x1 filter, no padding
+        # the batch's output pixels tiled as one range, A loaded by im2col TMA
+        # across rows and images: tiles that straddle images, part-empty last
+        # tiles (a last CTA entirely past the batch), corners of every sign
+        ((3, 64, 20, 20), 64, (3, 3), (1, 1), torch.float16),    # 400 pixels per image
+        ((4, 32, 22, 28), 40, (3, 3), (2, 1), torch.float16),    # pad_h != pad_w, 24 x 28 outputs, N tail
+        ((6, 64, 24, 26), 320, (3, 3), (1, 1), torch.bfloat16),  # 624 per image, two N tiles
+        ((2, 64, 40, 23), 64, (5, 5), (2, 2), torch.float16),    # 5x5 taps, odd width
+        ((2, 128, 32, 33), 96, (1, 1), (0, 0), torch.bfloat16),  # 1x1, no padding: upper corner 0
+        ((2, 64, 30, 30), 64, (3, 3), (0, 0), torch.float16),    # no padding: upper corner -2
     ],
 )
 def test_conv2d_tile_and_tap_edges(nchw, k, rs, pad, dtype):
