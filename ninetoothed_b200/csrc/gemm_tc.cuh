@@ -204,9 +204,16 @@ __device__ __forceinline__ void store_accumulator(const Params &prm, uint32_t tm
       if (!pix_ok || nc >= prm.N) continue;
       const int valid = (int)(prm.N - nc < 32 ? prm.N - nc : 32);
       TO *dst = pix + nc * prm.conv_osk;
+      if (prm.conv_osk == 1) {  // channels-last output: the pixel's 32 channels are one run
+        float v[32];
 #pragma unroll
-      for (int e = 0; e < 32; ++e)
-        if (e < valid) dst[e * prm.conv_osk] = from_f<TO>(round_f16(__uint_as_float(raw[e])));
+        for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
+        store_row_chunk<TO>(dst, v, valid == 32 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0, valid);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (e < valid) dst[e * prm.conv_osk] = from_f<TO>(round_f16(__uint_as_float(raw[e])));
+      }
     }
   } else {
     const int64_t m = row0 + row_in_tile;
@@ -1100,12 +1107,16 @@ int try_conv(const ConvProblem &p, void *workspace, int64_t workspace_bytes, cud
                       p.s - 1 - p.pad_w <= 128 && p.r <= 255 && p.s <= 255 && p.n * p.h * p.w * p.c * 2 >= 131072 &&
                       p.n * p.P * p.Q < (1LL << 31) - 2 * tile_m && encode_im2col_fn() != nullptr;
     const int64_t wp_stage = flat ? p.w : wp, pad_w_stage = flat ? 0 : p.pad_w;
-    T *act = static_cast<T *>(workspace);
+    // a dense channels-last (NHWC) input is already what the im2col map
+    // reads: only the filter is staged
+    const bool nhwc_input = flat && p.is[1] == 1 && p.is[3] == p.c && p.is[2] == p.w * p.c &&
+                            p.is[0] == p.h * p.w * p.c && (reinterpret_cast<uintptr_t>(p.input) & 15u) == 0;
+    T *act = nhwc_input ? const_cast<T *>(static_cast<const T *>(p.input)) : static_cast<T *>(workspace);
     T *flt = reinterpret_cast<T *>(static_cast<uint8_t *>(workspace) + ((p.n * p.h * wp * p.c * 2 + 255) / 256) * 256);
     {
       const int HW = (int)(p.h * p.w);
       // z-plane 0: the filter; planes 1 .. n: the images
-      dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)(p.n + 1));
+      dim3 grid((unsigned)((HW + 63) / 64), (unsigned)((p.c + 63) / 64), (unsigned)(nhwc_input ? 1 : p.n + 1));
       const FilterStaging<T> filter{static_cast<const T *>(p.filter), flt, (int)p.k, (int)p.c, (int)p.r, (int)p.s,
                                     p.fs[0], p.fs[1], p.fs[2], p.fs[3]};
       const bool dense_planes = p.is[3] == 1 && p.is[2] == p.w && HW % 8 == 0 && p.is[1] % 8 == 0 &&

@@ -434,6 +434,24 @@ def test_conv2d_tile_and_tap_edges(nchw, k, rs, pad, dtype):
     assert_within_steps(_np(y), ref, dtype, abs_sum=bound)
 
 
+@pytest.mark.parametrize("nchw, k, pad", [((4, 64, 28, 28), 128, (1, 1)), ((3, 32, 24, 30), 72, (2, 0))])
+def test_conv2d_channels_last_layouts(nchw, k, pad):
+    # a dense channels-last input feeds the im2col map directly (no staging
+    # copy); a channels-last output takes 16-byte stores; every combination
+    # must equal the NCHW result bit for bit (same products, same order)
+    gen = torch.Generator().manual_seed(sum(nchw) + k)
+    x = torch.randn(nchw, generator=gen).half().to(DEV)
+    w = (torch.randn((k, nchw[1], 3, 3), generator=gen) * 0.1).half().to(DEV)
+    ref = programs.conv2d(x, w, padding=pad)
+    x_cl = x.contiguous(memory_format=torch.channels_last)
+    assert torch.equal(programs.conv2d(x_cl, w, padding=pad), ref)
+    for inp in (x, x_cl):
+        out = torch.empty_like(ref, memory_format=torch.channels_last)
+        programs.conv2d_kernel(inp, w, out, padding_h=pad[0], padding_w=pad[1])
+        assert torch.equal(out, ref)
+    assert device_status() == 0
+
+
 @pytest.mark.parametrize("rows, cols, chunks", [(4096, 4096, 8), (1000, 781, 3), (5, 256, 8), (1, 64, 1)])
 def test_softmax_host_streaming_matches_device_softmax(rows, cols, chunks):
     # host in, host out, rows streamed in chunks over two CUDA streams
