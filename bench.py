@@ -55,6 +55,7 @@ def parse_args():
     p.add_argument("--soak-seconds", type=float, default=1.0,
                    help="untimed back-to-back steps before the timed region (clock samples cover both)")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="duration of the CPU-baseline sample")
+    p.add_argument("--reference-cpu-path-rows", type=int, default=None, help=argparse.SUPPRESS)
     p.add_argument("--only", default=None, choices=sorted(SINGLE_OPS),
                    help="run W + K launches of one op on its BASELINE shape (for profiling) and exit")
     return p.parse_args()
@@ -254,6 +255,76 @@ def run_reference(args, dist):
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+REFERENCE_INSTALL = REPO / "baseline" / "_ref"
+
+
+def reference_cpu_path_run(rows):
+    """Child-process body of `reference_cpu_path`: the reference's own softmax
+    program (its tests/test_softmax.py `softmax`, unmodified, from the copy in
+    baseline/_ref) under the Triton interpreter on `rows` rows of the workload,
+    then the torch CPU op that test compares with (torch.softmax) on a larger
+    sample with all host threads.  Harness settings only: TRITON_INTERPRET=1, a
+    CPU platform profile so the runtime accepts CPU tensors, and the in-memory
+    fix of the `dtype.value` read the interpreter's dtypes lack."""
+    import tempfile
+    import types
+
+    os.environ["TRITON_INTERPRET"] = "1"
+    os.environ["NINETOOTHED_PLATFORM"] = "cpu-interpret"
+    os.environ.setdefault("NINETOOTHED_CACHE_DIR", tempfile.mkdtemp(prefix="nt-ref-cpu-"))
+    sys.path.insert(0, str(REFERENCE_INSTALL))
+    tests_pkg = types.ModuleType("tests")  # the reference's test modules import each other as tests.<name>
+    tests_pkg.__path__ = [str(REFERENCE_INSTALL / "reference_tests")]
+    sys.modules["tests"] = tests_pkg
+    import ninetoothed.backends.emitters.triton as triton_emitter
+    from ninetoothed.targets import PlatformProfile, default_platform_registry
+
+    default_platform_registry().register(
+        PlatformProfile(name="cpu-interpret", device_types=("cpu",), backend_modes={"triton": {"jit"}}))
+    triton_emitter._RUNTIME_REDUCTION_IDENTITY = triton_emitter._RUNTIME_REDUCTION_IDENTITY.replace(
+        "dtype = dtype.value", "dtype = getattr(dtype, 'value', dtype)")
+    import tests.test_softmax as ref_softmax
+
+    x = (torch.randn((max(rows, 2048), COLS), generator=torch.Generator().manual_seed(2)) * 2).half()
+    ref_softmax.softmax(x[:1])  # builds and caches the kernel for BLOCK_SIZE = 4096
+    t0 = time.perf_counter()
+    out = ref_softmax.softmax(x[:rows])
+    interp_s = time.perf_counter() - t0
+    check = float((out.float() - torch.softmax(x[:rows].float(), -1)).abs().max())
+    threads = torch.get_num_threads()
+    torch.softmax(x.float(), -1).half()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 2.0:
+        torch.softmax(x.float(), -1).half()
+        n += 1
+    torch_s = (time.perf_counter() - t0) / n
+    print(json.dumps({
+        "interpreter": {"value": 2 * rows * COLS * 2 / interp_s / 1e9, "unit": "GB/s", "cores": 1,
+                        "sample": f"{rows} rows x {COLS} fp16 in {interp_s:.2f} s, reference tests/test_softmax.py "
+                                  "softmax under TRITON_INTERPRET=1", "max_abs_err_vs_torch": check},
+        "torch_cpu": {"value": 2 * x.shape[0] * COLS * 2 / torch_s / 1e9, "unit": "GB/s", "cores": threads,
+                      "sample": f"{x.shape[0]} rows x {COLS}, torch.softmax(x.float(), -1).half(), {n} passes"},
+    }), flush=True)
+
+
+def reference_cpu_path(rows=4, timeout=300):
+    """The reference's CPU path beside the oracle baseline: its softmax kernel
+    under the Triton interpreter and the torch CPU op (a child process, so the
+    interpreter setting stays out of this one)."""
+    if not (REFERENCE_INSTALL / "ninetoothed").is_dir() or not (REFERENCE_INSTALL / "reference_tests").is_dir():
+        return {"unavailable": "reference install baseline/_ref missing"}
+    try:
+        proc = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--reference-cpu-path-rows", str(rows)],
+                              capture_output=True, text=True, timeout=timeout, cwd=str(REPO))
+        last = proc.stdout.strip().splitlines()[-1] if proc.stdout.strip() else ""
+        if proc.returncode != 0 or not last.startswith("{"):
+            return {"unavailable": (proc.stderr.strip().splitlines() or ["no output"])[-1][:200]}
+        return json.loads(last)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"sample exceeded {timeout} s"}
 
 
 def cpu_baseline_sample(seconds=10.0):
@@ -501,6 +572,7 @@ def run_b200(args, dist):
     status = device_status()
 
     cpu = cpu_baseline_sample(args.cpu_seconds) if (dist.rank == 0 and dist.world == 1) else None
+    ref_cpu = reference_cpu_path() if (dist.rank == 0 and dist.world == 1 and args.cpu_seconds > 0) else None
     if dist.rank == 0:
         line = {
             "metric": "softmax_fp16_16384x4096_GB/s",
@@ -527,6 +599,7 @@ def run_b200(args, dist):
                 "algorithmic_bytes_per_launch": SOFTMAX_BYTES,
             },
             "cpu_baseline": cpu,
+            "cpu_reference_path": ref_cpu,
             "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": ROWS * COLS * 2,
                     "d2h_bytes_per_step": ROWS * COLS * 2, "ms_per_step": e2e_ms,
                     "runs_ms_per_step": e2e_runs, "api": "programs.softmax_host"},
@@ -541,6 +614,9 @@ def run_b200(args, dist):
 
 def main():
     args = parse_args()
+    if args.reference_cpu_path_rows is not None:
+        reference_cpu_path_run(args.reference_cpu_path_rows)
+        return 0
     if args.only:
         run_single(args)
         return 0
