@@ -141,11 +141,12 @@ struct Params {
   int *pool_counters;
 };
 
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int &mb, int &nb) {
-  const int per_group = GROUP_M * tiles_n;
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int &mb, int &nb,
+                                            int group_m = GROUP_M) {
+  const int per_group = group_m * tiles_n;
   const int group = tile / per_group;
-  const int first_m = group * GROUP_M;
-  const int gsize = min(tiles_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int gsize = min(tiles_m - first_m, group_m);
   const int in_group = tile % per_group;
   mb = first_m + in_group % gsize;
   nb = in_group / gsize;
@@ -447,8 +448,27 @@ constexpr int CTRL_BYTES = 256 + 8 * RING;
 constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + CTRL_BYTES;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 static_assert(8 * (2 * STAGES + 4) + 8 + 12 <= 256, "control block");
-__host__ __device__ constexpr int threads_for(Epilogue e) {
-  return e == Epilogue::kConvPool ? THREADS + 32 * POOL_WARPS : THREADS;
+// MB = 128-row blocks of A per CTA.  MB = 1: 256 x 256 pair tiles, 7-stage ring,
+// two accumulators in TMEM (the epilogue of one tile overlaps the next).
+// MB = 2: 512 x 256 pair tiles, each staged B block feeding two MMAs (one per
+// A block), 4-stage ring of 48 KB, one accumulator set of 2 x 256 columns
+// drained by two epilogue warpgroups side by side: a third less L2 -> SM
+// traffic per FLOP.
+template <int MB>
+struct PairCfg {
+  static constexpr int STAGES = MB == 1 ? 7 : 4;
+  static constexpr int A_STAGE_BYTES = MB * BM * 128;
+  static constexpr int NBUF = MB == 1 ? 2 : 1;  // accumulator sets of MB x BN columns
+  static constexpr int GROUP_M = 16 / MB;       // raster groups of 4096 A rows
+  static constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + CTRL_BYTES;
+  static_assert(NBUF * MB * BN <= TMEM_COLS, "TMEM columns");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+
+// MB = 2 doubles the epilogue: warps 2-5 drain A block 0's accumulator,
+// warps 6-9 A block 1's, side by side.
+__host__ __device__ constexpr int threads_for(Epilogue e, int mb = 1) {
+  return e == Epilogue::kConvPool ? THREADS + 32 * POOL_WARPS : THREADS + (mb - 1) * 128;
 }
 
 using gemm::Params;
@@ -621,10 +641,16 @@ __device__ __forceinline__ void pool_worker(const Params &prm, const PoolRing &r
   }
 }
 
-template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(EPI), 1)
+template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR, int MB>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_for(EPI, MB), 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                  Params prm) {
+  static_assert(MB == 1 || !is_conv(EPI), "conv tiles are 256 positions");
+  constexpr int STAGES = PairCfg<MB>::STAGES;
+  constexpr int A_STAGE_BYTES = PairCfg<MB>::A_STAGE_BYTES;
+  constexpr int NBUF = PairCfg<MB>::NBUF;
+  constexpr int GROUP = PairCfg<MB>::GROUP_M;
+  constexpr int TILE_M = 2 * BM * MB;  // rows of a pair tile
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = ptx::smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;  // same offset in both CTAs
@@ -653,7 +679,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(tfull_bar(b), 1);
-      ptx::mbar_init(tempty_bar(b), 8);  // one arrival per epilogue warp of both CTAs
+      ptx::mbar_init(tempty_bar(b), 8 * MB);  // one arrival per epilogue warp of both CTAs
     }
     *abort_flag = 0;
     if constexpr (EPI == Epilogue::kConvPool) {
@@ -685,8 +711,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += pairs) {
         int mb, nb;
-        gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
-        const int m0 = mb * (2 * BM) + (int)rank * BM;   // this CTA's rows of A
+        gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb, GROUP);
+        const int m0 = mb * TILE_M + (int)rank * (MB * BM);  // this CTA's rows of A
         const int n0 = nb * BN + (int)rank * BN_CTA;     // this CTA's half of B
         // conv: image and first position of this CTA's rows; flat tiling
         // splits the first output pixel into (image, p, q) once per tile
@@ -724,7 +750,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
                                     pos_a + (r - prm.conv_pad_h) * prm.conv_wp + sx, img_a);
             ptx::tma_load_3d_pair(b_dst, &tmap_b, fb, cb * gemm::BK, rs, n0);
           } else {
-            ptx::tma_load_2d_pair(a_dst, &tmap_a, fb, k0, m0);
+#pragma unroll
+            for (int h = 0; h < MB; ++h) ptx::tma_load_2d_pair(a_dst + h * (BM * 128), &tmap_a, fb, k0, m0 + h * BM);
             if constexpr (B_MN_MAJOR) {
 #pragma unroll
               for (int j = 0; j < BN_CTA / kblock<TI>(); ++j)
@@ -752,11 +779,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       int local = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += pairs, ++local) {
-        const int buf = local & 1;
-        const uint32_t use = (uint32_t)(local >> 1) & 1u;
+        const int buf = local % NBUF;
+        const uint32_t use = (uint32_t)(local / NBUF) & 1u;
         if (!ptx::mbar_wait(tempty_bar(buf), use ^ 1u, abort_flag)) break;
         ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * MB * BN);  // A block h accumulates at + h * BN
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!ptx::mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
           ptx::tc_fence_after();
@@ -764,16 +791,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           const uint32_t b_addr = b_base + stage * B_STAGE_BYTES;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {  // 4 x 32 bytes of K
-            const uint64_t a_desc = ptx::sw128_desc(a_addr + kk * 32, 16, 1024);
             uint64_t b_desc;
             if constexpr (B_MN_MAJOR)
               b_desc = ptx::sw128_desc(b_addr + kk * mma_k<TI>() * 128, kblock<TI>() * 128, 1024);
             else
               b_desc = ptx::sw128_desc(b_addr + kk * 32, 16, 1024);
-            if constexpr (sizeof(TI) == 1)
-              ptx::mma_f8_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
-            else
-              ptx::mma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < MB; ++h) {
+              const uint64_t a_desc = ptx::sw128_desc(a_addr + h * (BM * 128) + kk * 32, 16, 1024);
+              const uint32_t d = d_tmem + (uint32_t)(h * BN);
+              if constexpr (sizeof(TI) == 1)
+                ptx::mma_f8_ss_pair(d, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+              else
+                ptx::mma_f16_ss_pair(d, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
           }
           ptx::mma_commit_pair_both(empty_bar(stage));
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -781,24 +812,25 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         if (ok) ptx::mma_commit_pair_both(tfull_bar(buf));
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + 4 * MB) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    const int h = (warp - 2) >> 2;  // A block whose accumulator this warp drains
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += pairs, ++local) {
-      const int buf = local & 1;
-      const uint32_t use = (uint32_t)(local >> 1) & 1u;
+      const int buf = local % NBUF;
+      const uint32_t use = (uint32_t)(local / NBUF) & 1u;
       if (!ptx::mbar_wait_warp(tfull_bar(buf), use, abort_flag)) break;
       ptx::tc_fence_after();
       int mb, nb;
-      gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb);
+      gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb, GROUP);
       if constexpr (is_conv(EPI))
         gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
                                              (int64_t)(mb % prm.conv_tiles_img) * (2 * BM) + rank * BM,
                                              (int64_t)nb * BN, mb / prm.conv_tiles_img);
       else
-        gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
-                                             (int64_t)mb * (2 * BM) + rank * BM, (int64_t)nb * BN, 0);
+        gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)((buf * MB + h) * BN), quarter, lane,
+                                             (int64_t)mb * TILE_M + rank * (MB * BM) + h * BM, (int64_t)nb * BN, 0);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(buf), 0));
@@ -832,11 +864,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 
 // Launches gemm_pair_kernel persistently: as many CTA pairs as can be resident
 // at once (74 on a full B200), or fewer when there are fewer pair tiles.
-template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
+template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR, int MB = 1>
 int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params &prm, cudaStream_t stream) {
-  auto kern = gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>;
-  constexpr int threads = gemm2::threads_for(EPI);
-  cudaError_t e = smem_optin<gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR>>(gemm2::SMEM_BYTES);
+  auto kern = gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR, MB>;
+  constexpr int threads = gemm2::threads_for(EPI, MB);
+  constexpr int smem = gemm2::PairCfg<MB>::SMEM_BYTES;
+  cudaError_t e = smem_optin<gemm2::gemm_pair_kernel<TI, TO, EPI, B_MN_MAJOR, MB>>(smem);
   if (e != cudaSuccess) return (int)e;
   static std::atomic<int> resident_pairs[64] = {};  // per device, filled on first use (any thread)
   int device = 0;
@@ -846,7 +879,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)sm_count(), 1, 1);
     cfg.blockDim = dim3(threads, 1, 1);
-    cfg.dynamicSmemBytes = gemm2::SMEM_BYTES;
+    cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr;
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = 2;
@@ -862,7 +895,7 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
   }
   const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
   const int grid_pairs = (int)(tiles < pairs ? tiles : pairs);
-  kern<<<2 * grid_pairs, threads, gemm2::SMEM_BYTES, stream>>>(ta, tb, prm);
+  kern<<<2 * grid_pairs, threads, smem, stream>>>(ta, tb, prm);
   return launch_status();
 }
 
@@ -907,12 +940,21 @@ int try_gemm(const GemmProblem &p, cudaStream_t stream) {
     prm.out = p.out; prm.som = p.som; prm.son = p.son;
     prm.bias = p.bias; prm.sim = p.sim; prm.sin = p.sin;
     prm.beta = p.beta; prm.alpha = p.alpha;
-    const int tile_m = pair ? 2 * BM : BM;
+    // 512-row pair tiles (MB = 2) for 16-bit inputs when they still give
+    // every CTA pair at least two tiles; 256-row ones otherwise (8-bit inputs
+    // halve the MMA time per k-block, and the 4-stage ring of the 512-row
+    // kernel then no longer covers the load latency)
+    const int64_t tiles_n = (p.N + BN - 1) / BN;
+    const bool wide = pair && E == 2 && ((p.M + 4 * BM - 1) / (4 * BM)) * tiles_n >= 2 * (sm_count() / 2);
+    const int tile_m = pair ? (wide ? 4 * BM : 2 * BM) : BM;
     prm.tiles_m = (int)((p.M + tile_m - 1) / tile_m);
-    prm.tiles_n = (int)((p.N + BN - 1) / BN);
+    prm.tiles_n = (int)tiles_n;
     prm.num_kb = (int)((p.K + KB - 1) / KB);
     const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
     if (tiles > (1LL << 30)) return kNotEligible;
+    if (wide)
+      return b_mn ? launch_pair<TI, TO, EPI, true, 2>(ta, tb, prm, stream)
+                  : launch_pair<TI, TO, EPI, false, 2>(ta, tb, prm, stream);
     if (pair)
       return b_mn ? launch_pair<TI, TO, EPI, true>(ta, tb, prm, stream)
                   : launch_pair<TI, TO, EPI, false>(ta, tb, prm, stream);

@@ -221,6 +221,43 @@ def test_matmul_fp8_against_oracle(dtype, mnk, rhs_transposed):
     assert_within_steps(_np(out), oracle.matmul(a, b, "float16"), torch.float16, abs_sum=bound)
 
 
+@pytest.mark.parametrize(
+    "mnk, dtype, rhs_transposed",
+    [
+        ((4700, 4900, 200), torch.bfloat16, False),  # 512-row pair tiles: last tile 92 rows, partial k-block
+        ((2600, 8192, 256), torch.bfloat16, True),  # transposed (K-major) rhs
+        ((4097, 4352, 136), torch.float16, True),    # one row in the last tile's first A block
+    ],
+)
+def test_matmul_512_row_pair_tiles_sampled_rows(mnk, dtype, rhs_transposed):
+    # problems with at least two 512 x 256 tiles per CTA pair take the kernel
+    # whose CTAs stage two 128-row A blocks against one B block; rows around
+    # every 128-row block edge of the first and last tiles are checked
+    m, n, k = mnk
+    gen = torch.Generator().manual_seed(m + n + k)
+    a = torch.randn((m, k), generator=gen).to(dtype)
+    b = torch.randn((n, k), generator=gen).to(dtype).t() if rhs_transposed else torch.randn((k, n), generator=gen).to(dtype)
+    out = programs.matmul(a.to(DEV), b.to(DEV)).cpu()
+    last = (m - 1) // 512 * 512
+    rows = sorted({r for r in (0, 1, 127, 128, 255, 256, 383, 384, 511, 512, last, last + 127, last + 128,
+                               last + 255, last + 256, m - 2, m - 1) if 0 <= r < m})
+    sel = torch.tensor(rows)
+    ref = oracle.matmul(a[sel], b, "float16")
+    bound = oracle.matmul(a[sel].float().abs(), b.float().abs(), "float32")
+    assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
+
+
+def test_addmm_512_row_pair_tiles_sampled_rows():
+    m, n, k = 4600, 4608, 192
+    gen = torch.Generator().manual_seed(11)
+    inp, a = torch.randn((m, n), generator=gen).half(), torch.randn((m, k), generator=gen).half()
+    b = torch.randn((k, n), generator=gen).half()
+    out = programs.addmm(inp.to(DEV), a.to(DEV), b.to(DEV), beta=0.6, alpha=0.9).cpu()
+    sel = torch.tensor([0, 127, 128, 255, 256, 511, 4095, 4096, 4223, 4224, 4351, 4352, 4599])
+    ref = oracle.addmm(inp[sel], a[sel], b, 0.6, 0.9, "float16")
+    assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=addmm_abs_sum(a[sel].float(), b.float(), 0.9))
+
+
 def test_addmm_fp8_against_oracle():
     dtype = torch.float8_e5m2
     inp, a = torch.randn(256, 320).to(dtype), torch.randn(256, 192).to(dtype)
