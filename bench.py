@@ -44,7 +44,8 @@ SOFTMAX_BYTES = 2 * ROWS * COLS * 2  # one fp16 read + one fp16 write per elemen
 SOFTMAX_BUFFERS = 4  # rotating input/output pairs: 1 GiB working set > 126 MB L2
 
 
-SINGLE_OPS = ("softmax", "matmul", "addmm", "attention", "attention_causal", "conv2d", "max_pool2d")
+SINGLE_OPS = ("softmax", "matmul", "addmm", "attention", "attention_causal", "conv2d", "max_pool2d", "elementwise")
+ELEMENTS = 1 << 27  # elementwise configs: 2^27 fp16 elements (256 MiB per tensor, > L2)
 
 
 def parse_args():
@@ -384,7 +385,7 @@ def bench_ops(which, steps, dist, peaks):
         else:
             achieved = work / (ms * 1e-3) / 1e9
         profile = {"addmm": "gemm", "matmul": "gemm", "attention": "attention", "conv2d": "conv2d",
-                   "max_pool2d": "max_pool2d"}[name.split("_")[0] if not name.startswith("max_pool2d") else "max_pool2d"]
+                   "max_pool2d": "max_pool2d", "add": None, "pow": None, "dropout": None}[name.split("_")[0] if not name.startswith("max_pool2d") else "max_pool2d"]
         profile = profile if traffic else None
         results[name] = {"value": achieved * dist.world, "per_gpu": achieved, "unit": unit, "ms": ms,
                          "frac": achieved / peak, "peak": peak,
@@ -419,6 +420,21 @@ def bench_ops(which, steps, dist, peaks):
         record("attention_bf16_causal", lambda i: programs.attention_kernel(q, k, v, True, o), full / 2, "TFLOP/s",
                peaks["bf16_tflops"], nsteps=max(2, steps // 2), warm=2)
         del q, k, v, o
+    if "elementwise" in which:
+        # the reference's add / pow / dropout programs (tests/test_add.py,
+        # test_pow.py, test_dropout.py) on 2^27 fp16 elements: HBM-bound
+        xa, xb = (randn(ELEMENTS, dtype=torch.float16) for _ in range(2))
+        xe = randn(ELEMENTS, dtype=torch.float16, scale=0.5)
+        xpos = xa.abs() + 0.5
+        yo = torch.empty_like(xa)
+        nbytes3, nbytes2 = 3 * ELEMENTS * 2, 2 * ELEMENTS * 2
+        record("add_fp16_2e27", lambda i: programs.add_kernel(xa, xb, yo), nbytes3, "GB/s", peaks["hbm_gbs"],
+               traffic=False)
+        record("pow_fp16_2e27", lambda i: programs.pow_kernel(xpos, xe, yo), nbytes3, "GB/s", peaks["hbm_gbs"],
+               traffic=False)
+        record("dropout_fp16_2e27", lambda i: programs.dropout_kernel(xa, 0.5, 1234 + i, yo), nbytes2, "GB/s",
+               peaks["hbm_gbs"], traffic=False)
+        del xa, xb, xe, xpos, yo
     if "conv2d" in which or "max_pool2d" in which:
         xs = [randn(64, 256, 56, 56, dtype=torch.float16) for _ in range(2)]
         w = randn(256, 256, 3, 3, dtype=torch.float16, scale=(2 / (256 * 9)) ** 0.5)
@@ -489,6 +505,18 @@ def run_single(args):
         y = torch.empty(64, 256, 56, 56, device=dev, dtype=torch.float16)
         fn = lambda: programs.conv2d_kernel(x, w, y, padding_h=1, padding_w=1)  # noqa: E731
         work, unit = 2.0 * 64 * 256 * 56 * 56 * 256 * 9, "TFLOP/s"
+    elif op == "elementwise":
+        xa, xb = (randn(ELEMENTS, dtype=torch.float16) for _ in range(2))
+        xe = randn(ELEMENTS, dtype=torch.float16, scale=0.5)
+        xpos = xa.abs() + 0.5
+        yo = torch.empty_like(xa)
+
+        def fn():
+            programs.add_kernel(xa, xb, yo)
+            programs.pow_kernel(xpos, xe, yo)
+            programs.dropout_kernel(xa, 0.5, 1234, yo)
+
+        work, unit = 8 * ELEMENTS * 2, "GB/s"
     else:
         x = randn(64, 256, 56, 56, dtype=torch.float16)
         y = torch.empty(64, 256, 28, 28, device=dev, dtype=torch.float16)
@@ -575,7 +603,7 @@ def run_b200(args, dist):
 
     which = set()
     if args.ops != "none":
-        which = {"addmm", "matmul", "attention", "conv2d", "max_pool2d"} if args.ops == "all" else set(
+        which = {"addmm", "matmul", "attention", "conv2d", "max_pool2d", "elementwise"} if args.ops == "all" else set(
             args.ops.split(","))
     ops = bench_ops(which, args.op_steps, dist, peaks) if which else {}
     status = device_status()

@@ -18,20 +18,40 @@ namespace elementwise {
 // run on the counter (offset, 0, 0, 0).  This is the generator behind Triton's
 // `tl.rand(seed, offset)` (triton/language/random.py, `philox_impl`,
 // `randint4x`, `uint_to_uniform_float`), which the reference dropout calls.
+// Each round's two 32 x 32 -> 64-bit products are taken whole (high and low
+// words from one wide multiply), and the last round computes only word 0.
 __device__ __forceinline__ uint32_t philox_first_word(uint32_t c0, uint32_t key_lo, uint32_t key_hi) {
   uint32_t c1 = 0, c2 = 0, c3 = 0;
   uint32_t k0 = key_lo, k1 = key_hi;
 #pragma unroll
-  for (int round = 0; round < 10; ++round) {
-    const uint32_t p0 = c0, p2 = c2;
-    c0 = __umulhi(0xCD9E8D57u, p2) ^ c1 ^ k0;
-    c2 = __umulhi(0xD2511F53u, p0) ^ c3 ^ k1;
-    c1 = 0xCD9E8D57u * p2;
-    c3 = 0xD2511F53u * p0;
+  for (int round = 0; round < 9; ++round) {
+    const uint64_t w1 = (uint64_t)0xCD9E8D57u * c2;
+    const uint64_t w0 = (uint64_t)0xD2511F53u * c0;
+    c0 = (uint32_t)(w1 >> 32) ^ c1 ^ k0;
+    c2 = (uint32_t)(w0 >> 32) ^ c3 ^ k1;
+    c1 = (uint32_t)w1;
+    c3 = (uint32_t)w0;
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;
   }
-  return c0;
+  return __umulhi(0xCD9E8D57u, c2) ^ c1 ^ k0;
+}
+
+// x / keep rounded once to fp32, for 16-bit-float x (normal in fp32) and keep
+// in (0, 1]: with y = RN(1 / keep), q0 = RN(x * y) is within an ulp of x / keep,
+// r = x - q0 * keep is exact (one FMA), and RN(q0 + r * y) is the correctly
+// rounded quotient (Markstein's theorem, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990), so the
+// result equals an IEEE division.  Wider inputs keep the plain division.
+template <typename T>
+__device__ __forceinline__ float scale_kept(float x, float keep, float inv_keep) {
+  if constexpr (sizeof(T) == 2 && Elem<T>::is_f16) {
+    const float q0 = x * inv_keep;
+    const float r = __fmaf_rn(-q0, keep, x);
+    return __fmaf_rn(r, inv_keep, q0);
+  } else {
+    return __fdiv_rn(x, keep);
+  }
 }
 
 // Maps a 32-bit word to [0, 1): reinterpret as int32, fold negatives with
@@ -87,6 +107,7 @@ __global__ void dropout_vec(const T *__restrict__ in, T *__restrict__ out, int64
   const V *vi = reinterpret_cast<const V *>(in);
   V *vo = reinterpret_cast<V *>(out);
   const float keep = 1.f - p;
+  const float inv_keep = __frcp_rn(keep);
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
     V x, z;
@@ -95,7 +116,7 @@ __global__ void dropout_vec(const T *__restrict__ in, T *__restrict__ out, int64
     for (int e = 0; e < V::N; ++e) {
       const uint32_t offset = static_cast<uint32_t>(i * V::N + e);
       const float r = uniform_from_word(philox_first_word(offset, key_lo, key_hi));
-      z.v[e] = from_f<T>(r > p ? __fdiv_rn(to_f(x.v[e]), keep) : 0.f);
+      z.v[e] = from_f<T>(r > p ? scale_kept<T>(to_f(x.v[e]), keep, inv_keep) : 0.f);
     }
     __stcs(reinterpret_cast<int4 *>(vo + i), *reinterpret_cast<int4 *>(&z));
   }

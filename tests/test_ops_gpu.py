@@ -140,6 +140,21 @@ def test_dropout_golden_bit_exact(name):
     np.testing.assert_array_equal(_np(out), g["output"].astype(np.float32))
 
 
+@pytest.mark.parametrize("p", [1e-7, 0.1, 0.25, 0.3, 1 / 3, 0.5, 0.7, 0.9, 0.99, 0.123456])
+def test_dropout_fp16_scale_equals_ieee_division_for_every_value(p):
+    # every finite float16 value (four times, so each is kept under some mask
+    # word): a kept element must be round_f16(x / (1 - p)) with the division
+    # done once in fp32, as in the reference application
+    bits = torch.arange(0, 1 << 16, dtype=torch.int32).to(torch.int16).view(torch.float16)
+    x = bits[torch.isfinite(bits)].repeat(4)
+    out = programs.dropout(x.to(DEV), p=p, seed=20240601).cpu()
+    keep = torch.tensor(1.0, dtype=torch.float32) - torch.tensor(p, dtype=torch.float32)
+    expected = (x.float() / keep).half()
+    kept = out != 0
+    assert torch.equal(out[kept].view(torch.int16), expected[kept].view(torch.int16))
+    assert bool((out[~kept] == 0).all()) and 0.3 * (1 - p) < kept.float().mean() < 1.5 * (1 - p) + 1e-3
+
+
 def test_dropout_large_matches_oracle_and_statistics():
     x = torch.randn(1 << 20, device=DEV).half()
     p, seed = 0.3, 987654321
