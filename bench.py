@@ -44,7 +44,8 @@ SOFTMAX_BYTES = 2 * ROWS * COLS * 2  # one fp16 read + one fp16 write per elemen
 SOFTMAX_BUFFERS = 4  # rotating input/output pairs: 1 GiB working set > 126 MB L2
 
 
-SINGLE_OPS = ("softmax", "matmul", "addmm", "attention", "attention_causal", "conv2d", "max_pool2d", "elementwise")
+SINGLE_OPS = ("softmax", "matmul", "addmm", "attention", "attention_causal", "conv2d", "max_pool2d", "elementwise",
+              "layout")
 ELEMENTS = 1 << 27  # elementwise configs: 2^27 fp16 elements (256 MiB per tensor, > L2)
 
 
@@ -385,7 +386,8 @@ def bench_ops(which, steps, dist, peaks):
         else:
             achieved = work / (ms * 1e-3) / 1e9
         profile = {"addmm": "gemm", "matmul": "gemm", "attention": "attention", "conv2d": "conv2d",
-                   "max_pool2d": "max_pool2d", "add": None, "pow": None, "dropout": None}[name.split("_")[0] if not name.startswith("max_pool2d") else "max_pool2d"]
+                   "max_pool2d": "max_pool2d", "add": None, "pow": None, "dropout": None, "clone": None,
+                   "to": None}[name.split("_")[0] if not name.startswith("max_pool2d") else "max_pool2d"]
         profile = profile if traffic else None
         results[name] = {"value": achieved * dist.world, "per_gpu": achieved, "unit": unit, "ms": ms,
                          "frac": achieved / peak, "peak": peak,
@@ -435,6 +437,28 @@ def bench_ops(which, steps, dist, peaks):
         record("dropout_fp16_2e27", lambda i: programs.dropout_kernel(xa, 0.5, 1234 + i, yo), nbytes2, "GB/s",
                peaks["hbm_gbs"], traffic=False)
         del xa, xb, xe, xpos, yo
+    if "layout" in which:
+        # the reference's layout programs (tests/test_clone.py,
+        # tests/test_jagged.py): a 256 MiB fp16 matrix cloned as is and
+        # transposed, and a jagged batch padded to its longest sequence
+        rows, cols = 16384, 8192
+        xm = randn(rows, cols, dtype=torch.float16)
+        ym, yt = torch.empty_like(xm), torch.empty(cols, rows, device=dev, dtype=torch.float16)
+        record("clone_fp16_16384x8192", lambda i: programs.clone_kernel(xm, ym), 2 * rows * cols * 2, "GB/s",
+               peaks["hbm_gbs"], traffic=False)
+        record("clone_transposed_fp16_8192x16384", lambda i: programs.clone_kernel(xm.t(), yt), 2 * rows * cols * 2,
+               "GB/s", peaks["hbm_gbs"], traffic=False)
+        del xm, ym, yt
+        lengths = torch.randint(1024, 2049, (64,), generator=torch.Generator().manual_seed(5))
+        inner = 2048
+        offsets = torch.cat([torch.zeros(1, dtype=torch.int64), lengths.cumsum(0)]).to(dev)
+        values = randn(int(lengths.sum()), inner, dtype=torch.float16)
+        jagged = torch.nested.nested_tensor_from_jagged(values, offsets)
+        padded = torch.empty(64, int(lengths.max()), inner, device=dev, dtype=torch.float16)
+        record("to_padded_tensor_fp16_b64_l2048_d2048",
+               lambda i: programs.to_padded_kernel(jagged, padded, padding=0.0),
+               (values.numel() + padded.numel()) * 2, "GB/s", peaks["hbm_gbs"], traffic=False)
+        del values, jagged, padded
     if "conv2d" in which or "max_pool2d" in which:
         xs = [randn(64, 256, 56, 56, dtype=torch.float16) for _ in range(2)]
         w = randn(256, 256, 3, 3, dtype=torch.float16, scale=(2 / (256 * 9)) ** 0.5)
@@ -517,6 +541,15 @@ def run_single(args):
             programs.dropout_kernel(xa, 0.5, 1234, yo)
 
         work, unit = 8 * ELEMENTS * 2, "GB/s"
+    elif op == "layout":
+        xm = randn(16384, 8192, dtype=torch.float16)
+        ym, yt = torch.empty_like(xm), torch.empty(8192, 16384, device=dev, dtype=torch.float16)
+
+        def fn():
+            programs.clone_kernel(xm, ym)
+            programs.clone_kernel(xm.t(), yt)
+
+        work, unit = 4 * xm.numel() * 2, "GB/s"
     else:
         x = randn(64, 256, 56, 56, dtype=torch.float16)
         y = torch.empty(64, 256, 28, 28, device=dev, dtype=torch.float16)
@@ -603,7 +636,7 @@ def run_b200(args, dist):
 
     which = set()
     if args.ops != "none":
-        which = {"addmm", "matmul", "attention", "conv2d", "max_pool2d", "elementwise"} if args.ops == "all" else set(
+        which = {"addmm", "matmul", "attention", "conv2d", "max_pool2d", "elementwise", "layout"} if args.ops == "all" else set(
             args.ops.split(","))
     ops = bench_ops(which, args.op_steps, dist, peaks) if which else {}
     status = device_status()

@@ -59,6 +59,69 @@ __global__ void __launch_bounds__(256) tiled_kernel(const E *__restrict__ in, E 
   }
 }
 
+// Transpose of 16-bit elements: out[c * out_pitch + r] = in[r * in_pitch + c]
+// (the input contiguous along c, the output along r).  A 64 x 64 tile per CTA
+// iteration: a thread loads 8 columns of two adjacent rows with two 16-byte
+// loads, interleaves them into 8 words of (row 2k, row 2k + 1) pairs in a
+// [column][row pair] tile of 32-bit words, then 8 lanes store a column's 64
+// rows as one 128-byte run.  The tile's 16-byte chunks are XOR-swizzled by
+// column / 8, so both passes are free of bank conflicts.  Tile edges move
+// element by element.
+__global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t *__restrict__ in, uint16_t *__restrict__ out,
+                                                          int64_t rows, int64_t cols, int64_t in_pitch,
+                                                          int64_t out_pitch) {
+  __shared__ __align__(16) uint32_t tile[64][32];  // [column][row pair]
+  const int t = threadIdx.x;
+  const int64_t tiles_c = (cols + 63) / 64;
+  for (int64_t tb = blockIdx.x; tb < tiles_c * ((rows + 63) / 64); tb += gridDim.x) {
+    const int64_t r0 = (tb / tiles_c) * 64, c0 = (tb % tiles_c) * 64;
+    {
+      const int rp = t / 8, pv = t % 8;  // row pair 0..31, column group 0..7
+      const int64_t r = r0 + 2 * rp, c = c0 + 8 * pv;
+      uint32_t wa[4] = {0, 0, 0, 0}, wb[4] = {0, 0, 0, 0};
+      if (c + 8 <= cols && r + 1 < rows) {
+        const uint4 a = __ldcs(reinterpret_cast<const uint4 *>(in + r * in_pitch + c));
+        const uint4 b = __ldcs(reinterpret_cast<const uint4 *>(in + (r + 1) * in_pitch + c));
+        wa[0] = a.x; wa[1] = a.y; wa[2] = a.z; wa[3] = a.w;
+        wb[0] = b.x; wb[1] = b.y; wb[2] = b.z; wb[3] = b.w;
+      } else {
+        uint16_t ea[8] = {}, eb[8] = {};
+        for (int e = 0; e < 8; ++e) {
+          if (c + e < cols && r < rows) ea[e] = in[r * in_pitch + c + e];
+          if (c + e < cols && r + 1 < rows) eb[e] = in[(r + 1) * in_pitch + c + e];
+        }
+        for (int j = 0; j < 4; ++j) {
+          wa[j] = (uint32_t)ea[2 * j] | ((uint32_t)ea[2 * j + 1] << 16);
+          wb[j] = (uint32_t)eb[2 * j] | ((uint32_t)eb[2 * j + 1] << 16);
+        }
+      }
+      const int word = ((rp / 4) ^ pv) * 4 + rp % 4;  // columns pv * 8 + e all have column / 8 == pv
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // word j of a load holds columns 2j (low half) and 2j + 1
+        tile[pv * 8 + 2 * j][word] = __byte_perm(wa[j], wb[j], 0x5410);
+        tile[pv * 8 + 2 * j + 1][word] = __byte_perm(wa[j], wb[j], 0x7632);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int v = t + 256 * i;
+      const int pp = v / 8, cv = v % 8;  // column 0..63, vector of 8 rows 0..7
+      const int64_t c = c0 + pp, r = r0 + 8 * cv;
+      if (c < cols) {
+        const uint4 val = *reinterpret_cast<const uint4 *>(&tile[pp][((cv ^ (pp / 8)) & 7) * 4]);
+        if (r + 8 <= rows) {
+          __stcs(reinterpret_cast<uint4 *>(out + c * out_pitch + r), val);
+        } else {
+          const uint16_t *e = reinterpret_cast<const uint16_t *>(&val);
+          for (int k = 0; k < 8 && r + k < rows; ++k) out[c * out_pitch + r + k] = e[k];
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 inline int64_t abs64(int64_t v) { return v < 0 ? -v : v; }
 
 template <int W>
@@ -97,6 +160,22 @@ inline int copy2d(const void *in, void *out, int64_t rows, int64_t cols, int64_t
     if ((bits & 3u) == 0) return launch_rows<4>(in, out, rows, row, ir, orow, stream);
     if ((bits & 1u) == 0) return launch_rows<2>(in, out, rows, row, ir, orow, stream);
     return launch_rows<1>(in, out, rows, row, ir, orow, stream);
+  }
+  if (es == 2 && (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    // a transpose of 16-bit elements: the input contiguous along one
+    // dimension, the output along the other, pitches of whole 16-byte units
+    const bool in_c_out_r = isc == 1 && osr == 1 && isr > 0 && osc > 0 && isr % 8 == 0 && osc % 8 == 0;
+    const bool in_r_out_c = isr == 1 && osc == 1 && isc > 0 && osr > 0 && isc % 8 == 0 && osr % 8 == 0;
+    if (in_c_out_r || in_r_out_c) {
+      // out[c * out_pitch + r] = in[r * in_pitch + c] with (rows, cols) swapped for the second case
+      const int64_t tr = in_c_out_r ? rows : cols, tc = in_c_out_r ? cols : rows;
+      const int64_t tiles = ((tr + 63) / 64) * ((tc + 63) / 64);
+      const int64_t cap = (int64_t)sm_count() * 8;
+      transpose16_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(
+          static_cast<const uint16_t *>(in), static_cast<uint16_t *>(out), tr, tc, in_c_out_r ? isr : isc,
+          in_c_out_r ? osc : osr);
+      return launch_status();
+    }
   }
   if ((cols + 31) / 32 > 0x7fffffffLL) return NT_B200_ERR_INVALID_ARGUMENT;
   switch (es) {

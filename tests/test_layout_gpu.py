@@ -109,3 +109,33 @@ def test_jagged_both_ragged_dims_against_oracle(ragged, dtype):
     got_rows = np.concatenate([_bits(c if ragged == 1 else c.t()) for c in x.unbind()], axis=0)
     src_rows = _bits(src) if ragged == 1 else _bits(src).transpose(0, 2, 1)
     np.testing.assert_array_equal(got_rows, oracle.jagged_expand(src_rows, offsets))
+
+
+@pytest.mark.parametrize(
+    "case",
+    [
+        "input_rows_contiguous_output_transposed",   # input fast along columns, output along rows
+        "input_transposed_output_rows_contiguous",   # the other orientation
+        "odd_extents_sliced_pitches",                # 1001 x 777 in wider buffers: partial tiles, odd row pairs
+        "one_row",
+    ],
+)
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+def test_clone_transposing_layouts(case, dtype):
+    # 16-bit transposes take a 64 x 64 shared-memory tile path with 16-byte
+    # loads and stores; the result must equal the input bit for bit
+    gen = torch.Generator().manual_seed(len(case))
+    if case == "input_rows_contiguous_output_transposed":
+        x = torch.randn(520, 72, generator=gen).to(dtype).to(DEV)
+        out = torch.empty(72, 520, device=DEV, dtype=dtype).t()
+    elif case == "input_transposed_output_rows_contiguous":
+        x = torch.randn(776, 1000, generator=gen).to(dtype).to(DEV).t()
+        out = torch.empty(1000, 776, device=DEV, dtype=dtype)
+    elif case == "odd_extents_sliced_pitches":
+        x = torch.randn(800, 1008, generator=gen).to(dtype).to(DEV)[:777, :1001].t()
+        out = torch.empty(1001, 784, device=DEV, dtype=dtype)[:, :777]
+    else:
+        x = torch.randn(64, 1, generator=gen).to(dtype).to(DEV).t()
+        out = torch.empty(64, 1, device=DEV, dtype=dtype).t()
+    got = programs.clone_kernel(x, out)
+    assert torch.equal(got.view(torch.int16), x.contiguous().view(torch.int16))
