@@ -264,6 +264,23 @@ void launch_to_padded(const void *values, const int64_t *offsets, int64_t batch,
   memcpy(&pad, &pad_bits, sizeof(E));
   const int64_t lines = batch * max_len;
   const unsigned grid = (unsigned)(lines < (1 << 19) ? lines : (1 << 19));
+  constexpr int64_t per = 16 / (int64_t)sizeof(E);  // elements per 16-byte word
+  const bool words = vs1 == 1 && os[2] == 1 && inner % per == 0 && vs0 % per == 0 && os[0] % per == 0 &&
+                     os[1] % per == 0 && (reinterpret_cast<uintptr_t>(values) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+  if (words) {
+    // the dense dimension is contiguous on both sides: lines move as 16-byte
+    // words, padding as the pad element repeated across a word
+    uint4 pad_word;
+    E rep[per];
+    for (int64_t k = 0; k < per; ++k) rep[k] = pad;
+    memcpy(&pad_word, rep, 16);
+    const int64_t o0 = os[0] / per, o1 = os[1] / per;
+    to_padded_kernel<uint4><<<grid, 256, 0, stream>>>(static_cast<const uint4 *>(values), offsets, batch, max_len,
+                                                      inner / per, vs0 / per, 1, pad_word,
+                                                      static_cast<uint4 *>(out), o0, o1, 1);
+    return;
+  }
   to_padded_kernel<E><<<grid, 256, 0, stream>>>(static_cast<const E *>(values), offsets, batch, max_len, inner, vs0,
                                                 vs1, pad, static_cast<E *>(out), os[0], os[1], os[2]);
 }

@@ -84,12 +84,12 @@ def test_jagged_expand_matches_reference_fixture(name):
     np.testing.assert_array_equal(dst.values().cpu().numpy(), g["output"])
 
 
+@pytest.mark.parametrize("inner", (19, 64))  # 64: lines of whole 16-byte words take the word path
 @pytest.mark.parametrize("ragged", (1, 2))
 @pytest.mark.parametrize("dtype", (torch.float32, torch.bfloat16, torch.int8, torch.float64))
-def test_jagged_both_ragged_dims_against_oracle(ragged, dtype):
+def test_jagged_both_ragged_dims_against_oracle(ragged, dtype, inner):
     gen = torch.Generator().manual_seed(ragged)
     lengths = [1, 37, 5, 130] if ragged == 1 else [3, 1, 64]
-    inner = 19
     comps = [(torch.randn((n, inner) if ragged == 1 else (inner, n), generator=gen) * 10).to(dtype) for n in lengths]
     x = torch.nested.nested_tensor([c.to(DEV) for c in comps], layout=torch.jagged)
     if int(x._ragged_idx) != ragged:
