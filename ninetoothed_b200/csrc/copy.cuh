@@ -290,6 +290,15 @@ void launch_expand(void *values, const int64_t *offsets, int64_t batch, int64_t 
                    const void *src, int64_t ss0, int64_t ss2, cudaStream_t stream) {
   const int64_t per_batch = sm_count() * 8 / batch + 1;
   const dim3 grid((unsigned)(per_batch < 1024 ? per_batch : 1024), (unsigned)batch);
+  constexpr int64_t per = 16 / (int64_t)sizeof(E);  // elements per 16-byte word
+  if (vs1 == 1 && ss2 == 1 && inner % per == 0 && vs0 % per == 0 && ss0 % per == 0 &&
+      (reinterpret_cast<uintptr_t>(values) & 15u) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    // the dense dimension is contiguous on both sides: lines as 16-byte words
+    jagged_expand_kernel<uint4><<<grid, 256, 0, stream>>>(static_cast<uint4 *>(values), offsets, inner / per,
+                                                          vs0 / per, 1, static_cast<const uint4 *>(src), ss0 / per,
+                                                          1);
+    return;
+  }
   jagged_expand_kernel<E><<<grid, 256, 0, stream>>>(static_cast<E *>(values), offsets, inner, vs0, vs1,
                                                     static_cast<const E *>(src), ss0, ss2);
 }
