@@ -152,8 +152,9 @@ max_pool2d_pairs_kernel(const T *__restrict__ in, T *__restrict__ out, int C, in
   }
 }
 
-// 3x3 window, stride 2, padding 1 (the BASELINE pooling after conv2d), 16- or
-// 32-bit elements, even row length, rows starting on a pair boundary.  Lane q
+// 3x3 window, stride 2, padding 1 (the pooling that follows conv2d in the
+// benchmark configuration), 16- or 32-bit elements, even row length, rows
+// starting on a pair boundary.  Lane q
 // loads the element pair (2q, 2q+1) of each input row as one vector and the
 // element 2q-1 as a scalar (an L1 hit: the neighbouring lane's pair), takes the
 // horizontal 3-max in the element type, and the vertical maxima over the 5
@@ -215,7 +216,7 @@ max_pool2d_3x3s2p1_kernel(const T *__restrict__ in, T *__restrict__ out, int C, 
 }
 
 // Vector form of the 3x3 / stride 2 / padding 1 path for 16-bit elements, row
-// length W <= 64 with W % 8 == 0 and Q % 4 == 0 (56 -> 28 in the BASELINE
+// length W <= 64 with W % 8 == 0 and Q % 4 == 0 (56 -> 28 in the benchmark
 // config).  An 8-lane group owns one pair of output rows: lane j loads input
 // columns [8j, 8j + 8) of each of the 5 input rows with one 16-byte load,
 // takes column 8j - 1 from lane j - 1 by a shuffle, and writes output

@@ -1,6 +1,6 @@
 """Work partitioning across the GPUs of one node (one process per GPU).
 
-Every BASELINE program shards with no reduction: matmul/addmm by output rows
+Every benchmarked program shards with no reduction: matmul/addmm by output rows
 (each rank holds its rows of A/bias and a replica of B), attention by
 (batch x head) pairs, conv2d/max_pool2d by images, softmax by rows.  The only
 collective is an optional all-gather of the output shards over NCCL, which
