@@ -122,6 +122,50 @@ __global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t *__rest
   }
 }
 
+// Transpose of 32-bit elements, same contract as transpose16_kernel: a 32 x 32
+// tile per CTA iteration, one 16-byte load of 4 columns and one 16-byte store
+// of 4 rows per thread, through a [column][row] tile padded by one word per
+// column so that both passes spread over the banks.
+__global__ void __launch_bounds__(256) transpose32_kernel(const uint32_t *__restrict__ in, uint32_t *__restrict__ out,
+                                                          int64_t rows, int64_t cols, int64_t in_pitch,
+                                                          int64_t out_pitch) {
+  __shared__ uint32_t tile[32][33];  // [column][row]
+  const int t = threadIdx.x;
+  const int64_t tiles_c = (cols + 31) / 32;
+  for (int64_t tb = blockIdx.x; tb < tiles_c * ((rows + 31) / 32); tb += gridDim.x) {
+    const int64_t r0 = (tb / tiles_c) * 32, c0 = (tb % tiles_c) * 32;
+    {
+      const int rr = t / 8, cv = t % 8;  // row 0..31, group of 4 columns 0..7
+      const int64_t r = r0 + rr, c = c0 + 4 * cv;
+      uint32_t w[4] = {0, 0, 0, 0};
+      if (r < rows && c + 4 <= cols) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4 *>(in + r * in_pitch + c));
+        w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+      } else if (r < rows) {
+        for (int e = 0; e < 4; ++e)
+          if (c + e < cols) w[e] = in[r * in_pitch + c + e];
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[4 * cv + e][rr] = w[e];
+    }
+    __syncthreads();
+    {
+      const int cc = t / 8, rv = t % 8;  // column 0..31, group of 4 rows 0..7
+      const int64_t c = c0 + cc, r = r0 + 4 * rv;
+      if (c < cols) {
+        const uint4 v = make_uint4(tile[cc][4 * rv], tile[cc][4 * rv + 1], tile[cc][4 * rv + 2], tile[cc][4 * rv + 3]);
+        if (r + 4 <= rows) {
+          __stcs(reinterpret_cast<uint4 *>(out + c * out_pitch + r), v);
+        } else {
+          const uint32_t e4[4] = {v.x, v.y, v.z, v.w};
+          for (int k = 0; k < 4 && r + k < rows; ++k) out[c * out_pitch + r + k] = e4[k];
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 inline int64_t abs64(int64_t v) { return v < 0 ? -v : v; }
 
 template <int W>
@@ -173,6 +217,20 @@ inline int copy2d(const void *in, void *out, int64_t rows, int64_t cols, int64_t
       const int64_t cap = (int64_t)sm_count() * 8;
       transpose16_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(
           static_cast<const uint16_t *>(in), static_cast<uint16_t *>(out), tr, tc, in_c_out_r ? isr : isc,
+          in_c_out_r ? osc : osr);
+      return launch_status();
+    }
+  }
+  if (es == 4 && (reinterpret_cast<uintptr_t>(in) & 15u) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+    // the same for 32-bit elements, pitches of whole 16-byte units
+    const bool in_c_out_r = isc == 1 && osr == 1 && isr > 0 && osc > 0 && isr % 4 == 0 && osc % 4 == 0;
+    const bool in_r_out_c = isr == 1 && osc == 1 && isc > 0 && osr > 0 && isc % 4 == 0 && osr % 4 == 0;
+    if (in_c_out_r || in_r_out_c) {
+      const int64_t tr = in_c_out_r ? rows : cols, tc = in_c_out_r ? cols : rows;
+      const int64_t tiles = ((tr + 31) / 32) * ((tc + 31) / 32);
+      const int64_t cap = (int64_t)sm_count() * 8;
+      transpose32_kernel<<<(unsigned)(tiles < cap ? tiles : cap), 256, 0, stream>>>(
+          static_cast<const uint32_t *>(in), static_cast<uint32_t *>(out), tr, tc, in_c_out_r ? isr : isc,
           in_c_out_r ? osc : osr);
       return launch_status();
     }

@@ -120,9 +120,9 @@ def test_jagged_both_ragged_dims_against_oracle(ragged, dtype, inner):
         "one_row",
     ],
 )
-@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16, torch.float32))
 def test_clone_transposing_layouts(case, dtype):
-    # 16-bit transposes take a 64 x 64 shared-memory tile path with 16-byte
+    # 16- and 32-bit transposes take shared-memory tile paths with 16-byte
     # loads and stores; the result must equal the input bit for bit
     gen = torch.Generator().manual_seed(len(case))
     if case == "input_rows_contiguous_output_transposed":
@@ -138,4 +138,5 @@ def test_clone_transposing_layouts(case, dtype):
         x = torch.randn(64, 1, generator=gen).to(dtype).to(DEV).t()
         out = torch.empty(64, 1, device=DEV, dtype=dtype).t()
     got = programs.clone_kernel(x, out)
-    assert torch.equal(got.view(torch.int16), x.contiguous().view(torch.int16))
+    bits = torch.int32 if dtype == torch.float32 else torch.int16
+    assert torch.equal(got.contiguous().view(bits), x.contiguous().view(bits))
