@@ -111,6 +111,42 @@ rows_in_registers(const T *__restrict__ input, T *__restrict__ output, int64_t r
   }
 }
 
+// Unit column stride, any row length and alignment: the row in registers as
+// EPT scalars per thread (element j * THREADS + t), loaded and stored with
+// coalesced scalar accesses, so a row is still read from HBM once.
+template <typename T, int THREADS, int EPT>
+__global__ void __launch_bounds__(THREADS)
+rows_in_registers_scalar(const T *__restrict__ input, T *__restrict__ output, int64_t rows, int64_t cols,
+                         int64_t in_row_stride, int64_t out_row_stride) {
+  __shared__ float red[32];
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T *src = input + row * in_row_stride;
+    T *dst = output + row * out_row_stride;
+    float x[EPT];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const int64_t c = (int64_t)j * THREADS + threadIdx.x;
+      x[j] = c < cols ? to_f(__ldcs(src + c)) : -INFINITY;
+      m = fmaxf(m, x[j]);
+    }
+    m = block_reduce_max<THREADS>(m, red);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      x[j] = fast_exp<T>(x[j] - m);
+      s += x[j];
+    }
+    s = block_reduce_sum<THREADS>(s, red);
+    const float inv = 1.f / s;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) {
+      const int64_t c = (int64_t)j * THREADS + threadIdx.x;
+      if (c < cols) __stcs(dst + c, from_f<T>(x[j] * inv));
+    }
+  }
+}
+
 // General path for any strides and lengths: three passes over the row with
 // scalar loads (the second and third hit L2 for rows that fit there).
 template <typename T, int THREADS>
@@ -158,6 +194,16 @@ int run(const void *input, void *output, int64_t rows, int64_t cols, int64_t isr
   } else if (aligned && nvec <= 256 * 8) {
     if (nvec <= 256 * 4) launch_regs<T, 256, 4>(in, out, rows, cols, isr, osr, stream);
     else launch_regs<T, 256, 8>(in, out, rows, cols, isr, osr, stream);
+  } else if (isc == 1 && osc == 1 && cols <= 256 * 16) {
+    const int64_t grid = rows < (1 << 30) ? rows : (1 << 30);
+    if (cols <= 128 * 4)
+      rows_in_registers_scalar<T, 128, 4><<<(unsigned)grid, 128, 0, stream>>>(in, out, rows, cols, isr, osr);
+    else if (cols <= 256 * 4)
+      rows_in_registers_scalar<T, 256, 4><<<(unsigned)grid, 256, 0, stream>>>(in, out, rows, cols, isr, osr);
+    else if (cols <= 256 * 8)
+      rows_in_registers_scalar<T, 256, 8><<<(unsigned)grid, 256, 0, stream>>>(in, out, rows, cols, isr, osr);
+    else
+      rows_in_registers_scalar<T, 256, 16><<<(unsigned)grid, 256, 0, stream>>>(in, out, rows, cols, isr, osr);
   } else {
     const int64_t grid = rows < (1 << 30) ? rows : (1 << 30);
     rows_strided<T, 256><<<(unsigned)grid, 256, 0, stream>>>(in, out, rows, cols, isr, isc, osr, osc);

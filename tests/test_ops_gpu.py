@@ -85,7 +85,9 @@ def test_softmax_reference_test_case():
     np.testing.assert_allclose(_np(y), oracle.softmax(x, "float32"), rtol=1e-5, atol=1e-8)
 
 
-@pytest.mark.parametrize("shape", ((1, 1), (3, 8), (5, 4104), (7, 33000), (2, 65536)))
+@pytest.mark.parametrize("shape", ((1, 1), (3, 8), (5, 4104), (7, 33000), (2, 65536),
+                                   # rows of any length in registers with scalar loads
+                                   (6, 515), (4, 1027), (9, 2049), (3, 4095)))
 def test_softmax_ragged_and_long_rows(shape):
     x = torch.randn(shape).half()
     y = programs.softmax(x.to(DEV))
