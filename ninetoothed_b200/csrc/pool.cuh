@@ -297,6 +297,61 @@ inline void launch_pairs(const T *in, T *out, int64_t n, int64_t c, int64_t h, i
       in, out, (int)c, (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], (int)ph, (int)pw);
 }
 
+// 2x2 window, stride 2, no padding, 16-bit elements, W % 8 == 0: a thread
+// takes 8 columns of input rows 2p and 2p + 1 with two 16-byte loads and writes
+// the 4 outputs with one 8-byte store (row 2p + 1 past the input, as the last
+// output row of an odd height in ceil mode, reads as -inf).
+template <typename T>
+__global__ void __launch_bounds__(256)
+max_pool2d_2x2s2_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int P, int vecs,
+                            int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp,
+                            int64_t total) {
+  using V = typename Pair<T>::V;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int v = (int)(i % vecs);
+    const int64_t row = i / vecs;
+    const int p = (int)(row % P);
+    const int64_t nc = row / P;
+    const int ci = (int)(nc % C);
+    const int64_t ni = nc / C;
+    const T *r0 = in + ni * isn + ci * isc + (int64_t)(2 * p) * ish + 8 * v;
+    uint4 a = __ldcs(reinterpret_cast<const uint4 *>(r0));
+    uint4 b;
+    if (2 * p + 1 < H) {
+      b = __ldcs(reinterpret_cast<const uint4 *>(r0 + ish));
+    } else {
+      const T ninf = neg_inf<T>();
+      const unsigned short bits = *reinterpret_cast<const unsigned short *>(&ninf);
+      const uint32_t w2 = (uint32_t)bits | ((uint32_t)bits << 16);
+      b = make_uint4(w2, w2, w2, w2);
+    }
+    const V *va = reinterpret_cast<const V *>(&a);
+    const V *vb = reinterpret_cast<const V *>(&b);
+    alignas(8) T o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const V m = __hmax2(va[k], vb[k]);  // vertical max of columns 2k, 2k + 1
+      const T *mm = reinterpret_cast<const T *>(&m);
+      o[k] = __hmax(mm[0], mm[1]);
+    }
+    *reinterpret_cast<uint2 *>(out + ni * osn + ci * osc + (int64_t)p * osp + 4 * v) = *reinterpret_cast<const uint2 *>(o);
+  }
+}
+
+template <typename T>
+inline void launch_2x2s2_vec(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
+                             int64_t P, const int64_t *os, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    const int64_t total = n * c * P * (w / 8);
+    int64_t grid = (total + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (grid > cap) grid = cap;
+    max_pool2d_2x2s2_vec_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(in, out, (int)c, (int)h, (int)P, (int)(w / 8),
+                                                                       is[0], is[1], is[2], os[0], os[1], os[2],
+                                                                       total);
+  }
+}
+
 template <typename T, int WH, int WW, int SH, int SW>
 inline void launch_rows(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
                         int64_t P, int64_t Q, const int64_t *os, int64_t wh, int64_t ww, int64_t sh, int64_t sw,
@@ -355,6 +410,12 @@ extern "C" int nt_b200_max_pool2d(const void *input, void *output, int64_t n, in
                                                                     os[2]);
       } else if (window_h == 3 && window_w == 3 && stride_h == 2 && stride_w == 2)
         nt::pool::launch_pairs<T, 3, 3, 2, 2>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
+      else if (sizeof(T) == 2 && window_h == 2 && window_w == 2 && stride_h == 2 && stride_w == 2 && pad_h == 0 &&
+               pad_w == 0 && w % 8 == 0 && out_w * 2 == w && is[2] % 8 == 0 && is[1] % 8 == 0 && is[0] % 8 == 0 &&
+               os[2] % 4 == 0 && os[1] % 4 == 0 && os[0] % 4 == 0 &&
+               (reinterpret_cast<uintptr_t>(input) & 15u) == 0 && (reinterpret_cast<uintptr_t>(output) & 7u) == 0) {
+        nt::pool::launch_2x2s2_vec<T>(in, out, n, c, h, w, is, out_h, os, s);
+      }
       else if (window_h == 3 && window_w == 3 && stride_h == 3 && stride_w == 3)
         nt::pool::launch_pairs<T, 3, 3, 3, 3>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
       else if (window_h == 2 && window_w == 2 && stride_h == 2 && stride_w == 2)

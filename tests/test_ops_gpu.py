@@ -197,6 +197,17 @@ def test_max_pool2d_3x3_s2_p1_edges(dtype, ceil_mode, hw):
     assert torch.equal(y, F.max_pool2d(x, 3, 2, 1, ceil_mode=ceil_mode))
 
 
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16, torch.float32))
+@pytest.mark.parametrize("ceil_mode", (False, True))
+@pytest.mark.parametrize("hw", ((56, 56), (57, 64), (8, 8), (9, 10)))
+def test_max_pool2d_2x2_s2(dtype, ceil_mode, hw):
+    # 16-bit inputs with W % 8 == 0 take the 16-byte vector path (an odd last
+    # row in ceil mode reads as -inf); the others the row-pair path
+    x = torch.randn((3, 5, *hw), device=DEV).to(dtype)
+    y = programs.max_pool2d(x, (2, 2), ceil_mode=ceil_mode, stride=2)
+    assert torch.equal(y, F.max_pool2d(x, 2, 2, ceil_mode=ceil_mode))
+
+
 @pytest.mark.parametrize("name", golden_io.names("max_pool2d_"))
 def test_max_pool2d_golden(name):
     g = golden_io.load(name)
