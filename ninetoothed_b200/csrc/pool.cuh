@@ -338,6 +338,70 @@ max_pool2d_2x2s2_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C
   }
 }
 
+// 3x3 window, stride 3, no padding (the reference test's default: stride =
+// window), 16-bit elements: a thread computes 8 outputs of one output row from
+// the 24 input columns under them, three 16-byte loads per input row when the
+// segment lies inside the row, element loads with -inf past the row's end or
+// below the last input row (ceil mode) otherwise; the 8 outputs leave as one
+// 16-byte store when they are all in the row and aligned.
+template <typename T>
+__global__ void __launch_bounds__(256)
+max_pool2d_3x3s3_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
+                            int groups, int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc,
+                            int64_t osp, bool out_vec, int64_t total) {
+  const T ninf = neg_inf<T>();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int g = (int)(i % groups);
+    const int64_t row = i / groups;
+    const int p = (int)(row % P);
+    const int64_t nc = row / P;
+    const int ci = (int)(nc % C);
+    const int64_t ni = nc / C;
+    const T *plane = in + ni * isn + ci * isc;
+    const int x0 = 24 * g;
+    alignas(16) T o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = ninf;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const int y = 3 * p + r;
+      if (y >= H) break;
+      const T *irow = plane + (int64_t)y * ish + x0;
+      alignas(16) T seg[24];
+      if (x0 + 24 <= W) {
+#pragma unroll
+        for (int u = 0; u < 3; ++u) reinterpret_cast<uint4 *>(seg)[u] = __ldcs(reinterpret_cast<const uint4 *>(irow) + u);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 24; ++e) seg[e] = x0 + e < W ? irow[e] : ninf;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = __hmax(o[k], __hmax(__hmax(seg[3 * k], seg[3 * k + 1]), seg[3 * k + 2]));
+    }
+    T *orow = out + ni * osn + ci * osc + (int64_t)p * osp + 8 * g;
+    if (out_vec && 8 * g + 8 <= Q) {
+      *reinterpret_cast<uint4 *>(orow) = *reinterpret_cast<const uint4 *>(o);
+    } else {
+      for (int k = 0; k < 8 && 8 * g + k < Q; ++k) orow[k] = o[k];
+    }
+  }
+}
+
+template <typename T>
+inline void launch_3x3s3_vec(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
+                             int64_t P, int64_t Q, const int64_t *os, bool out_vec, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    const int64_t groups = (Q + 7) / 8;
+    const int64_t total = n * c * P * groups;
+    int64_t grid = (total + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (grid > cap) grid = cap;
+    max_pool2d_3x3s3_vec_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(in, out, (int)c, (int)h, (int)w, (int)P, (int)Q,
+                                                                       (int)groups, is[0], is[1], is[2], os[0], os[1],
+                                                                       os[2], out_vec, total);
+  }
+}
+
 template <typename T>
 inline void launch_2x2s2_vec(const T *in, T *out, int64_t n, int64_t c, int64_t h, int64_t w, const int64_t *is,
                              int64_t P, const int64_t *os, cudaStream_t stream) {
@@ -416,6 +480,13 @@ extern "C" int nt_b200_max_pool2d(const void *input, void *output, int64_t n, in
                (reinterpret_cast<uintptr_t>(input) & 15u) == 0 && (reinterpret_cast<uintptr_t>(output) & 7u) == 0) {
         nt::pool::launch_2x2s2_vec<T>(in, out, n, c, h, w, is, out_h, os, s);
       }
+      else if (sizeof(T) == 2 && window_h == 3 && window_w == 3 && stride_h == 3 && stride_w == 3 && pad_h == 0 &&
+               pad_w == 0 && is[2] % 8 == 0 && is[1] % 8 == 0 && is[0] % 8 == 0 &&
+               (reinterpret_cast<uintptr_t>(input) & 15u) == 0)
+        nt::pool::launch_3x3s3_vec<T>(in, out, n, c, h, w, is, out_h, out_w, os,
+                                      os[2] % 8 == 0 && os[1] % 8 == 0 && os[0] % 8 == 0 &&
+                                          (reinterpret_cast<uintptr_t>(output) & 15u) == 0,
+                                      s);
       else if (window_h == 3 && window_w == 3 && stride_h == 3 && stride_w == 3)
         nt::pool::launch_pairs<T, 3, 3, 3, 3>(in, out, n, c, h, w, is, out_h, out_w, os, pad_h, pad_w, s);
       else if (window_h == 2 && window_w == 2 && stride_h == 2 && stride_w == 2)

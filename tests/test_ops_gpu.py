@@ -208,6 +208,17 @@ def test_max_pool2d_2x2_s2(dtype, ceil_mode, hw):
     assert torch.equal(y, F.max_pool2d(x, 2, 2, ceil_mode=ceil_mode))
 
 
+@pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16, torch.float32))
+@pytest.mark.parametrize("ceil_mode", (False, True))
+@pytest.mark.parametrize("hw", ((64, 64), (56, 56), (10, 25), (9, 8), (31, 48)))
+def test_max_pool2d_3x3_s3(dtype, ceil_mode, hw):
+    # the reference test's default (stride = window); 16-bit inputs take the
+    # path with 24-column segments per thread, partial at the row's end
+    x = torch.randn((3, 5, *hw), device=DEV).to(dtype)
+    y = programs.max_pool2d(x, (3, 3), ceil_mode=ceil_mode)
+    assert torch.equal(y, F.max_pool2d(x, 3, 3, ceil_mode=ceil_mode))
+
+
 @pytest.mark.parametrize("name", golden_io.names("max_pool2d_"))
 def test_max_pool2d_golden(name):
     g = golden_io.load(name)
