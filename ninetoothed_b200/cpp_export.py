@@ -143,16 +143,19 @@ def _body(program, a):
             f"const int64_t n = {shape(0, 0)}, c = {shape(0, 1)}, h = {shape(0, 2)}, w = {shape(0, 3)};",
             f"const int64_t k = {shape(1, 0)}, r = {shape(1, 2)}, s = {shape(1, 3)};",
             f"const int64_t is[4] = {a.strides(0, 4)}, fs[4] = {a.strides(1, 4)}, os[4] = {a.strides(2, 4)};",
-            "// staging from the library's fixed array; a larger problem gets a",
-            "// stream-ordered workspace for the duration of the call",
-            f"int rc = nt_b200_conv2d_no_alloc({args}, {code(0)}, stream);",
-            "if (rc != NT_B200_ERR_WORKSPACE_TOO_LARGE) return rc;",
+            "// staging workspace of this call alone, stream-ordered (cudaMallocAsync",
+            "// neither synchronises the device nor is shared with other calls), so",
+            "// launches on different streams or host threads never touch each other's",
+            "// memory, as with the reference's own AOT launch functions",
             f"const int64_t bytes = nt_b200_conv2d_workspace_size(n, c, h, w, k, r, s, {ph}, {pw}, {code(0)});",
             "void *workspace = nullptr;",
-            "cudaError_t e = cudaMallocAsync(&workspace, static_cast<size_t>(bytes), static_cast<cudaStream_t>(stream));",
-            "if (e != cudaSuccess) return static_cast<int>(e);",
-            f"rc = nt_b200_conv2d({args}, workspace, bytes, {code(0)}, stream);",
-            "e = cudaFreeAsync(workspace, static_cast<cudaStream_t>(stream));",
+            "if (bytes > 0) {",
+            "  const cudaError_t e = cudaMallocAsync(&workspace, static_cast<size_t>(bytes), "
+            "static_cast<cudaStream_t>(stream));",
+            "  if (e != cudaSuccess) return static_cast<int>(e);",
+            "}",
+            f"const int rc = nt_b200_conv2d({args}, workspace, bytes, {code(0)}, stream);",
+            "const cudaError_t e = workspace ? cudaFreeAsync(workspace, static_cast<cudaStream_t>(stream)) : cudaSuccess;",
             "return rc != 0 ? rc : static_cast<int>(e);",
         ]
     if program == "max_pool2d":

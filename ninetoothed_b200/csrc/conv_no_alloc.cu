@@ -20,9 +20,11 @@
 //     safe.  The staging writes every byte it later reads, so the contents left
 //     by the previous call never leak into a result;
 //   - the device address of the array is looked up (cudaGetSymbolAddress) the
-//     first time the entry point runs on a device, with that device current;
-//     make that first call before any stream capture begins, and do not use
-//     the entry point on a device after cudaDeviceReset in the same process.
+//     first time the entry point runs on a device, with that device current,
+//     and again on later calls until a lookup succeeds; make that first call
+//     before any stream capture begins, and do not use the entry point on a
+//     device after cudaDeviceReset in the same process.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -39,25 +41,38 @@ constexpr int kMaxDevices = 64;
 // is only a stand-in, not a device address; use scratch_address().
 static __device__ __align__(256) uint8_t g_conv_scratch[kConvStaticWorkspaceBytes];
 
+// The address is published through an atomic once a lookup has succeeded; a
+// failed lookup (say, a first call made while the device's context could not
+// be created) is not remembered, so a later call on that device tries again.
 struct DeviceScratch {
-  std::once_flag once;
-  void *address = nullptr;
-  cudaError_t status = cudaSuccess;
+  std::mutex lock;
+  std::atomic<void *> address{nullptr};
 };
 
 static DeviceScratch g_device_scratch[kMaxDevices];
 
-// Device address of g_conv_scratch on the current device, looked up once per
-// device.  Returns 0 or an error code.
+// Device address of g_conv_scratch on the current device, looked up with that
+// device current until one lookup succeeds.  Returns 0 or an error code.
 static int scratch_address(void **out) {
   int device = 0;
   const cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (device < 0 || device >= kMaxDevices) return NT_B200_ERR_NO_DEVICE;
   DeviceScratch &slot = g_device_scratch[device];
-  std::call_once(slot.once, [&slot] { slot.status = cudaGetSymbolAddress(&slot.address, g_conv_scratch); });
-  if (slot.status != cudaSuccess) return static_cast<int>(slot.status);
-  *out = slot.address;
+  void *address = slot.address.load(std::memory_order_acquire);
+  if (address == nullptr) {
+    std::lock_guard<std::mutex> guard(slot.lock);
+    address = slot.address.load(std::memory_order_acquire);
+    if (address == nullptr) {
+      const cudaError_t status = cudaGetSymbolAddress(&address, g_conv_scratch);
+      if (status != cudaSuccess || address == nullptr) {
+        cudaGetLastError();  // the failed lookup leaves no sticky error behind for the caller's next launch
+        return static_cast<int>(status != cudaSuccess ? status : cudaErrorInvalidSymbol);
+      }
+      slot.address.store(address, std::memory_order_release);
+    }
+  }
+  *out = address;
   return 0;
 }
 

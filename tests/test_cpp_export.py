@@ -75,6 +75,11 @@ def _premake_addmm(dtype):
                                             Tensor(2, dtype=ninetoothed.float16))
 
 
+def _premake_conv2d(dtype):
+    cv = ref.load("test_conv2d")
+    return cv.premake(dtype=dtype)
+
+
 def _compile(cpp, out_dir):
     """The exported sources built as a shared library, the way a C++ host
     would build them (ninetoothed.h and <kernel>.h beside the source)."""
@@ -120,6 +125,15 @@ def test_build_writes_and_compiles_the_tensor_abi_entry_point(nt, tmp_path):
     library = _compile(cpp, tmp_path)
     _lib, fn = _launcher(library, "mm_export", 3)
     assert fn is not None
+
+
+def test_exported_conv2d_takes_a_workspace_of_its_own(nt, tmp_path):
+    """The exported conv2d wrapper stages through a stream-ordered workspace of
+    its own call, not the library's shared fixed array, so concurrent launches
+    on different streams stay independent."""
+    source = _build(nt, _premake_conv2d, nt.float16, "conv_export", tmp_path).read_text()
+    assert "cudaMallocAsync(" in source and "cudaFreeAsync(" in source
+    assert "nt_b200_conv2d(" in source and "nt_b200_conv2d_no_alloc" not in source
 
 
 def test_runtime_dtypes_get_no_export(nt, tmp_path):
@@ -180,3 +194,25 @@ def test_exported_kernels_run_from_the_tensor_abi(nt, tmp_path):
     assert add(stream, tx, ty, tz_null) == 10001              # null data
     big = (ctypes.c_uint64 * 1)(2**63)
     assert add(stream, NineToothedTensor(tx.data, big, tx.strides), ty, tz) == 10001  # extent > INT64_MAX
+
+
+@pytest.mark.gpu
+def test_exported_conv2d_runs_from_the_tensor_abi(nt, tmp_path):
+    """Two conv2d problems through the exported wrapper, one with staging under
+    64 MiB and one above it, each against F.conv2d; return code 0."""
+    import torch.nn.functional as F
+
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    gen = torch.Generator(device=dev).manual_seed(9)
+    lib_cv, cv = _launcher(_compile(_build(nt, _premake_conv2d, nt.float16, "conv_run", tmp_path), tmp_path),
+                           "conv_run", 3)
+    for n, c, h, w, k in ((2, 64, 20, 24, 128), (32, 256, 64, 64, 64)):
+        x = torch.randn(n, c, h, w, device=dev, generator=gen).half()
+        f = (torch.randn(k, c, 3, 3, device=dev, generator=gen) * (2 / (9 * c)) ** 0.5).half()
+        y = torch.empty(n, k, h - 2, w - 2, device=dev, dtype=torch.float16)
+        (tx, k1), (tf, k2), (ty, k3) = _tensor(x), _tensor(f), _tensor(y)
+        assert cv(stream, tx, tf, ty) == 0
+        torch.cuda.synchronize()
+        expected = F.conv2d(x.float(), f.float())
+        torch.testing.assert_close(y.float(), expected, rtol=1e-2, atol=1e-2)

@@ -286,6 +286,22 @@ def test_matmul_512_row_pair_tiles_sampled_rows(mnk, dtype, rhs_transposed):
     assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
 
 
+def test_matmul_baseline_config_sampled_rows():
+    # BASELINE matmul: bf16 8192^3, entries N(0, 1) / sqrt(8192), fp16 output
+    # (the application's cast), B row-major (MN-major for the MMA): the
+    # 512 x 256 pair-tile kernel with a 128-k-block main loop.  Rows around
+    # 128-row block edges of the first, a middle and the last tile.
+    s = 8192
+    gen = torch.Generator().manual_seed(8192)
+    a = (torch.randn((s, s), generator=gen) * s ** -0.5).bfloat16()
+    b = (torch.randn((s, s), generator=gen) * s ** -0.5).bfloat16()
+    out = programs.matmul(a.to(DEV), b.to(DEV)).cpu()
+    sel = torch.tensor([0, 1, 127, 128, 255, 256, 383, 511, 512, 4095, 4096, 4097, 7680, 8063, 8064, 8191])
+    ref = oracle.matmul(a[sel], b, "float16")
+    bound = oracle.matmul(a[sel].abs(), b.abs(), "float32")
+    assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
+
+
 def test_addmm_512_row_pair_tiles_sampled_rows():
     m, n, k = 4600, 4608, 192
     gen = torch.Generator().manual_seed(11)
@@ -565,3 +581,15 @@ def test_conv2d_max_pool2d_equals_the_two_programs(nchw, k, rs, pad, dtype, insi
     assert torch.equal(fused, two)  # bit-identical
     again = programs.conv2d_max_pool2d(x, w, padding=pad, pool_in_conv_kernel=inside)  # counters restart per call
     assert torch.equal(again, two)
+    # and against the oracle: conv (same cast chain) then the pool.  Max over
+    # a window moves by at most the largest difference inside it, so the
+    # conv's per-element tolerance, max-pooled, bounds the pooled difference.
+    name = "float16" if dtype == torch.float16 else "bfloat16"
+    conv_ref = oracle.conv2d(x.cpu(), w.cpu(), pad, name)
+    bound = oracle.conv2d(x.cpu().abs(), w.cpu().abs(), pad, "float32")
+    tol = 2 * _steps(conv_ref, dtype) + 1e-6 + bound * 2.0 ** -20
+    out_hw = tuple(fused.shape[2:])
+    pooled_ref = oracle.max_pool2d(conv_ref, (3, 3), out_hw, stride=(2, 2), padding=(1, 1))
+    pooled_tol = oracle.max_pool2d(tol, (3, 3), out_hw, stride=(2, 2), padding=(1, 1))
+    err = np.abs(_np(fused) - pooled_ref)
+    assert (err <= pooled_tol).all(), f"max err {err.max()}"

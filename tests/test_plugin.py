@@ -173,9 +173,18 @@ def test_other_platforms_keep_the_stock_cuda_backend(nt):
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", ["matmul", "addmm", "attention", "conv2d", "max_pool2d", "dropout", "pow"])
 def test_make_runs_reference_program_on_b200(nt, name):
+    """A handle from the reference's `make()` gives the `programs` result bit
+    for bit, and both agree with the CPU oracle within the tolerance of the
+    kernel-level tests (so a fault shared by both CUDA paths is caught)."""
+    import numpy as np
     import torch.nn.functional as F
 
+    import oracle
     from ninetoothed_b200 import programs
+    from tests.test_ops_gpu import addmm_abs_sum, assert_within_steps
+
+    def host(t):
+        return t.detach().float().cpu().numpy()
 
     arrangement, application, tensors = _programs(nt)[name]
     kernel = nt.make(arrangement, application, tensors, backend="cuda", platform="nvidia-b200")
@@ -185,36 +194,48 @@ def test_make_runs_reference_program_on_b200(nt, name):
         out = torch.empty(256, 320, device=dev, dtype=torch.float16)
         kernel(a, b, out)
         assert torch.equal(out, programs.matmul(a, b))
+        bound = oracle.matmul(a.cpu().abs(), b.cpu().abs(), "float32")
+        assert_within_steps(host(out), oracle.matmul(a.cpu(), b.cpu(), "float16"), torch.float16, abs_sum=bound)
     elif name == "addmm":
         i, a, b = (torch.randn(256, 256, device=dev).half() for _ in range(3))
         out = torch.empty(256, 256, device=dev, dtype=torch.float16)
         kernel(i, a, b, 0.5, 0.75, out)
         assert torch.equal(out, programs.addmm(i, a, b, 0.5, 0.75))
+        ref = oracle.addmm(i.cpu(), a.cpu(), b.cpu(), 0.5, 0.75, "float16")
+        assert_within_steps(host(out), ref, torch.float16, abs_sum=addmm_abs_sum(a.cpu().float(), b.cpu().float(), 0.75))
     elif name == "attention":
         q, k, v = (torch.randn(2, 4, 256, 64, device=dev).half() for _ in range(3))
         o = torch.empty_like(q)
         kernel(q, k, v, True, o)
         assert torch.allclose(o, F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=1), atol=1e-2, rtol=1e-2)
+        ref = oracle.attention(q.cpu(), k.cpu(), v.cpu(), True, "float16")
+        np.testing.assert_allclose(host(o), ref, rtol=1e-2, atol=1e-2)
     elif name == "conv2d":
         x, w = torch.rand(2, 64, 16, 16, device=dev).half(), torch.rand(128, 64, 3, 3, device=dev).half()
         out = torch.empty(2, 128, 16, 16, device=dev, dtype=torch.float16)
         kernel(x, w, out, padding_h=1, padding_w=1)
         assert torch.equal(out, programs.conv2d(x, w, padding=1))
+        bound = oracle.conv2d(x.cpu().abs(), w.cpu().abs(), (1, 1), "float32")
+        ref = oracle.conv2d(x.cpu(), w.cpu(), (1, 1), "float16")
+        assert_within_steps(host(out), ref, torch.float16, abs_sum=bound)
     elif name == "max_pool2d":
         x = torch.randn(4, 3, 16, 16, device=dev).half()
         out = torch.empty(4, 3, 5, 5, device=dev, dtype=torch.float16)
         kernel(x, out, WINDOW_HEIGHT=3, WINDOW_WIDTH=3)
         assert torch.equal(out, F.max_pool2d(x, 3))
+        np.testing.assert_array_equal(host(out), oracle.max_pool2d(x.cpu(), (3, 3), (5, 5)))
     elif name == "dropout":
         x = torch.randn(1000, device=dev).half()
         out = torch.empty_like(x)
         kernel(x, 0.3, 1234, out)
         assert torch.equal(out, programs.dropout(x, 0.3, 1234))
+        np.testing.assert_array_equal(host(out), oracle.dropout(x.cpu(), 0.3, 1234, "float16"))
     else:
         x, y = torch.rand(1000, device=dev), torch.rand(1000, device=dev)
         out = torch.empty_like(x)
         kernel(x, y, out)
         assert torch.equal(out, programs.pow(x, y))
+        np.testing.assert_allclose(host(out), oracle.pow(x.cpu(), y.cpu()), rtol=1e-6)
 
 
 # The reference's own operator tests (tests/test_*.py of the reference), run
@@ -232,20 +253,12 @@ REFERENCE_CASES = [
     ("test_max_pool2d", dict(n=32, c=3, h=64, w=64, r=3, s=3, dtype=torch.float16, ceil_mode=False)),
     ("test_max_pool2d", dict(n=32, c=3, h=64, w=64, r=3, s=3, dtype=torch.float16, ceil_mode=True)),
     ("test_addmm", dict(m=512, n=512, k=512, dtype=torch.float16, atol=0.075)),
-    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1024, emb_dim=64, dtype=torch.float16, is_causal=False,
-                            rtol=0.01, atol=0.01)),
-    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1024, emb_dim=64, dtype=torch.float16, is_causal=True,
-                            rtol=0.01, atol=0.01)),
-    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1, emb_dim=64, dtype=torch.float16, is_causal=True,
-                            rtol=0.01, atol=0.01)),
-    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1024, emb_dim=64, dtype=torch.float32, is_causal=True,
-                            rtol=0.025, atol=0.025)),
-    ("test_attention", dict(batch_size=2, num_heads=4, seq_len=1, emb_dim=64, dtype=torch.float32, is_causal=False,
-                            rtol=0.025, atol=0.025)),
-    ("test_conv2d", dict(n=4, c=64, h=16, w=16, k=512, r=3, s=3, padding=(1, 1), dtype=torch.float16, rtol=0.001,
-                         atol=0.001)),
-    ("test_conv2d", dict(n=4, c=64, h=16, w=16, k=512, r=3, s=3, padding=(2, 0), dtype=torch.float16, rtol=0.001,
-                         atol=0.001)),
+    # tests/test_attention.py:99-117: every (dtype, seq_len, is_causal) combination
+    *[("test_attention", dict(batch_size=2, num_heads=4, seq_len=seq, emb_dim=64, dtype=dtype, is_causal=causal,
+                              rtol=tol, atol=tol))
+      for dtype, tol in ((torch.float32, 0.025), (torch.float16, 0.01)) for seq in (1024, 1) for causal in (False, True)],
+    *[("test_conv2d", dict(n=4, c=64, h=16, w=16, k=512, r=3, s=3, padding=pad, dtype=torch.float16, rtol=0.001,
+                           atol=0.001)) for pad in (0, (1, 1), (0, 1), (2, 0))],
 ]
 
 

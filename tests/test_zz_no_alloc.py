@@ -12,9 +12,11 @@ stops at the first failure has run every other test first.
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
+import oracle
 from ninetoothed_b200 import _lib
 from ninetoothed_b200.runtime import device_status
 
@@ -63,12 +65,15 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
     stream = torch.cuda.current_stream(dev).cuda_stream
     gen = torch.Generator(device=dev).manual_seed(11)
     cases = [
-        # (image batch, channels, height, width, filters, padding, dtype)
-        ((4, 64, 16, 16), 128, (1, 1), torch.float16, FLOAT16),
-        ((2, 128, 14, 14), 256, (0, 1), torch.bfloat16, BFLOAT16),
+        # (image batch, channels, height, width, filters, padding, dtype, channels-last input)
+        ((4, 64, 16, 16), 128, (1, 1), torch.float16, FLOAT16, False),    # padded NCHW staging
+        ((2, 128, 14, 14), 256, (0, 1), torch.bfloat16, BFLOAT16, False),  # flat im2col staging
+        ((3, 64, 20, 20), 64, (1, 1), torch.float16, FLOAT16, True),       # only the filter is staged
     ]
-    for shape, filters, padding, dtype, code in cases:
+    for shape, filters, padding, dtype, code, channels_last in cases:
         x = torch.randn(shape, device=dev, generator=gen).to(dtype)
+        if channels_last:
+            x = x.contiguous(memory_format=torch.channels_last)
         w = (torch.randn((filters, shape[1], 3, 3), device=dev, generator=gen) * 0.05).to(dtype)
         expected = _with_workspace(lib, x, w, padding, code, stream)
         got = _no_alloc(lib, x, w, padding, code, stream)
@@ -76,6 +81,15 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
         # same kernels on the same staging layout: the tolerance of the conv2d
         # tests (rtol = atol = 1e-3) holds trivially
         assert torch.allclose(got.float(), expected.float(), rtol=1e-3, atol=1e-3)
+        # and an independent check against the CPU oracle (same cast chain,
+        # summation order aside): two rounding steps plus the fp32 order term
+        name = "float16" if dtype == torch.float16 else "bfloat16"
+        ref = oracle.conv2d(x.cpu(), w.cpu(), padding, name)
+        bound = oracle.conv2d(x.cpu().abs(), w.cpu().abs(), padding, "float32")
+        step = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32) if dtype == torch.float16 else \
+            np.abs(ref) * 2.0 ** -7 + 2.0 ** -133
+        tol = 2 * step + 1e-6 + bound * 2.0 ** -20
+        assert (np.abs(got.float().cpu().numpy() - ref) <= tol).all()
     assert device_status() == 0
 
 
