@@ -31,17 +31,29 @@ DTYPE_CODES = {"float16": 8, "bfloat16": 9, "float32": 10, "float8_e4m3fn": 12, 
 _lib = None
 
 
+# F16C makes the float16 conversions one instruction instead of a libgcc
+# software routine (about 15x faster overall); AVX2 and FMA are present on
+# every x86-64 host CPU of a B200 node.  -ffp-contract=off keeps every
+# multiply and add separately rounded, as written in oracle.c (explicit fmaf
+# calls stay fused), so the results do not depend on these flags.
+CFLAGS = ("-O3", "-mavx2", "-mfma", "-mf16c", "-ffp-contract=off", "-fopenmp", "-fPIC", "-shared", "-std=gnu11")
+
+
 def build(force: bool = False) -> Path:
-    """Compile oracle.c with gcc (-O2, OpenMP) into oracle/_build/liboracle.so."""
-    if not force and LIBRARY.is_file() and LIBRARY.stat().st_mtime >= SOURCE.stat().st_mtime:
+    """Compile oracle.c with gcc (OpenMP, F16C) into oracle/_build/liboracle.so."""
+    stamp = BUILD_DIR / "cflags.txt"
+    flags = " ".join(CFLAGS)
+    if (not force and LIBRARY.is_file() and LIBRARY.stat().st_mtime >= SOURCE.stat().st_mtime and stamp.is_file()
+            and stamp.read_text() == flags):
         return LIBRARY
     BUILD_DIR.mkdir(exist_ok=True)
     temporary = BUILD_DIR / f".liboracle.{os.getpid()}.tmp"
     subprocess.run(
-        ["gcc", "-O2", "-fopenmp", "-fPIC", "-shared", "-std=gnu11", "-o", str(temporary), str(SOURCE), "-lm"],
+        ["gcc", *CFLAGS, "-o", str(temporary), str(SOURCE), "-lm"],
         check=True,
     )
     os.replace(temporary, LIBRARY)
+    stamp.write_text(flags)
     return LIBRARY
 
 
