@@ -42,6 +42,7 @@ import statistics
 import subprocess
 import sys
 import time
+import warnings
 from pathlib import Path
 
 import torch
@@ -418,12 +419,20 @@ class OpTimer:
         graph = None
         if not eager:
             try:
-                graph = capture_steps(fn, nsteps)
+                with warnings.catch_warnings(record=True) as caught:
+                    warnings.simplefilter("always")
+                    graph = capture_steps(fn, nsteps)
+                # a launch path that launches on another stream than the
+                # capturing one leaves the graph empty (torch warns): time it
+                # eagerly instead
+                if any("Graph is empty" in str(w.message) for w in caught):
+                    graph = None
             except Exception:  # a launch path that cannot be captured: time it eagerly
                 torch.cuda.synchronize()
                 graph = None
+            if self.dist.max(0.0 if graph is not None else 1.0) > 0:  # every rank takes the same path
+                graph = None
         if graph is not None:
-            graph.replay()
             runs = timed_trials(lambda: time_graph(graph, self.stream), self.dist, OP_MIN_REGION_MS)
             del graph
             mode = "graph"
@@ -609,11 +618,11 @@ def bench_reference_gpu(tuning, steps, dist, ours):
             entry["vs_triton"] = ms / ours[ours_name]["ms"]
         results[name] = entry
 
-    x = (torch.randn((ROWS, COLS), generator=gen, device=dev) * 2).half()
-    xs = [x] + [torch.empty_like(x).copy_(x) for _ in range(3)]
-    record("softmax_fp16_16384x4096", "softmax_fp16_16384x4096", "softmax", lambda k, i: k(xs[i % 4]), SOFTMAX_BYTES,
-           "GB/s", nsteps=steps)
-    del x, xs
+    xs = [(torch.randn((ROWS, COLS), generator=gen, device=dev) * 2).half() for _ in range(4)]
+    ys = [torch.empty_like(x) for x in xs]
+    record("softmax_fp16_16384x4096", "softmax_fp16_16384x4096", "softmax", lambda k, i: k(xs[i % 4], ys[i % 4]),
+           SOFTMAX_BYTES, "GB/s", nsteps=steps)
+    del xs, ys
     a, b, c = (randn(GEMM, GEMM, dtype=torch.bfloat16, scale=GEMM ** -0.5) for _ in range(3))
     out16 = torch.empty(GEMM, GEMM, device=dev, dtype=torch.float16)
     out = torch.empty(GEMM, GEMM, device=dev, dtype=torch.bfloat16)

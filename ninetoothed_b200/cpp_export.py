@@ -104,6 +104,30 @@ class _Args:
         return str(default)
 
 
+def _call_workspace(size_expression):
+    """Statements that take the call's workspace: memory of this call alone,
+    stream-ordered (cudaMallocAsync neither synchronises the device nor is
+    shared with other calls), so launches on different streams or host threads
+    never touch each other's memory, as with the reference's own AOT launch
+    functions."""
+    return [
+        f"const int64_t bytes = {size_expression};",
+        "void *workspace = nullptr;",
+        "if (bytes > 0) {",
+        "  const cudaError_t e = cudaMallocAsync(&workspace, static_cast<size_t>(bytes), "
+        "static_cast<cudaStream_t>(stream));",
+        "  if (e != cudaSuccess) return static_cast<int>(e);",
+        "}",
+    ]
+
+
+def _free_workspace():
+    return [
+        "const cudaError_t e = workspace ? cudaFreeAsync(workspace, static_cast<cudaStream_t>(stream)) : cudaSuccess;",
+        "return rc != 0 ? rc : static_cast<int>(e);",
+    ]
+
+
 def _body(program, a):
     """Statements that compute and return the result of one program call."""
     shape, stride, code = a.shape, a.stride, a.code
@@ -143,20 +167,9 @@ def _body(program, a):
             f"const int64_t n = {shape(0, 0)}, c = {shape(0, 1)}, h = {shape(0, 2)}, w = {shape(0, 3)};",
             f"const int64_t k = {shape(1, 0)}, r = {shape(1, 2)}, s = {shape(1, 3)};",
             f"const int64_t is[4] = {a.strides(0, 4)}, fs[4] = {a.strides(1, 4)}, os[4] = {a.strides(2, 4)};",
-            "// staging workspace of this call alone, stream-ordered (cudaMallocAsync",
-            "// neither synchronises the device nor is shared with other calls), so",
-            "// launches on different streams or host threads never touch each other's",
-            "// memory, as with the reference's own AOT launch functions",
-            f"const int64_t bytes = nt_b200_conv2d_workspace_size(n, c, h, w, k, r, s, {ph}, {pw}, {code(0)});",
-            "void *workspace = nullptr;",
-            "if (bytes > 0) {",
-            "  const cudaError_t e = cudaMallocAsync(&workspace, static_cast<size_t>(bytes), "
-            "static_cast<cudaStream_t>(stream));",
-            "  if (e != cudaSuccess) return static_cast<int>(e);",
-            "}",
+            *_call_workspace(f"nt_b200_conv2d_workspace_size(n, c, h, w, k, r, s, {ph}, {pw}, {code(0)})"),
             f"const int rc = nt_b200_conv2d({args}, workspace, bytes, {code(0)}, stream);",
-            "const cudaError_t e = workspace ? cudaFreeAsync(workspace, static_cast<cudaStream_t>(stream)) : cudaSuccess;",
-            "return rc != 0 ? rc : static_cast<int>(e);",
+            *_free_workspace(),
         ]
     if program == "max_pool2d":
         wh, ww = a.meta("WINDOW_HEIGHT"), a.meta("WINDOW_WIDTH")

@@ -95,9 +95,7 @@ def build(name, tuning="short"):
     from ninetoothed import Tensor
 
     if name == "softmax":
-        # the reference's helper as it is: it builds its @ninetoothed.jit
-        # kernel and allocates the output on every call
-        return _SoftmaxHelper(ref.load("test_softmax"))
+        return _softmax_kernel(ref.load("test_softmax"))
     mm = ref.load("test_matmul")
     if name in ("matmul", "addmm", "conv2d"):
         overrides, options = _gemm_options(tuning)
@@ -141,16 +139,30 @@ def build(name, tuning="short"):
     raise ValueError(f"unknown program {name}")
 
 
-class _SoftmaxHelper:
-    """The reference's softmax helper (tests/test_softmax.py:10-27).
-    `helper(x)` returns its output as the reference does (one kernel launch);
-    `helper(x, y)` also copies it into `y` (a second, torch launch)."""
+def _softmax_kernel(module):
+    """The kernel handle the reference's softmax helper (tests/test_softmax.py:
+    10-27) builds with `@ninetoothed.jit`.  The helper builds it anew on every
+    call (about a second of compile-time Python each time), so one call is made
+    with `ninetoothed.jit` observed and the handle it returns is kept; it is
+    then called as the helper calls it, `kernel(input, output,
+    BLOCK_SIZE=cols)`."""
+    import torch
 
-    def __init__(self, module):
-        self.module = module
+    nt = module.ninetoothed
+    original = nt.jit
+    handles = []
 
-    def __call__(self, x, y=None):
-        out = self.module.softmax(x)
-        if y is not None:
-            y.copy_(out)
-        return out
+    def observe(func=None, **options):
+        handle = original(func, **options)
+        handles.append(handle)
+        return handle
+
+    nt.jit = observe
+    try:
+        module.softmax(torch.zeros((1, 16), device="cuda", dtype=torch.float16))
+    finally:
+        nt.jit = original
+    if len(handles) != 1:
+        raise RuntimeError("the reference softmax helper did not build exactly one kernel")
+    kernel = handles[0]
+    return lambda x, y: kernel(x, y, BLOCK_SIZE=x.shape[-1])

@@ -302,6 +302,79 @@ def test_matmul_baseline_config_sampled_rows():
     assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
 
 
+# The shards a multi-GPU split gives each GPU (ninetoothed_b200.sharding):
+# M-row shards of the BASELINE GEMM (1024 and 2048 rows of 8192 at 8 and 4
+# GPUs), whose tile plan differs from the whole problem's, and smaller
+# problems; rows across tile edges against the oracle, and a second call
+# bit-identical to the first.
+@pytest.mark.parametrize(
+    "mnk, dtype",
+    [
+        ((1024, 8192, 8192), torch.bfloat16),  # the 8-GPU row shard of the BASELINE matmul
+        ((2048, 4096, 2048), torch.float16),
+        ((4096, 2560, 1024), torch.bfloat16),
+        ((512, 1024, 4096), torch.bfloat16),
+        ((1000, 1000, 3000), torch.float16),   # ragged tiles, k-blocks and rows
+    ],
+)
+def test_matmul_row_shards(mnk, dtype):
+    m, n, k = mnk
+    gen = torch.Generator().manual_seed(m + n + k)
+    a = (torch.randn((m, k), generator=gen) * k ** -0.5).to(dtype)
+    b = torch.randn((k, n), generator=gen).to(dtype)
+    ad, bd = a.to(DEV), b.to(DEV)
+    out = programs.matmul(ad, bd)
+    assert torch.equal(programs.matmul(ad, bd), out)
+    rows = sorted({r for r in (0, 1, 127, 128, 255, 256, 257, 511, 512, m // 2, m - 129, m - 128, m - 2, m - 1)
+                   if 0 <= r < m})
+    sel = torch.tensor(rows)
+    ref = oracle.matmul(a[sel], b, "float16")
+    bound = oracle.matmul(a[sel].abs(), b.abs(), "float32")
+    assert_within_steps(out.cpu()[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
+
+
+def test_matmul_fp8_row_shard():
+    dtype = torch.float8_e5m2
+    m, n, k = 1024, 4096, 8192
+    gen = torch.Generator().manual_seed(3)
+    a = torch.randn((m, k), generator=gen).to(dtype)
+    b = torch.randn((n, k), generator=gen).to(dtype).t()
+    out = programs.matmul(a.to(DEV), b.to(DEV)).cpu()
+    sel = torch.tensor([0, 255, 256, 511, 700, 1023])
+    ref = oracle.matmul(a[sel], b, "float16")
+    bound = oracle.matmul(a[sel].float().abs(), b.float().abs(), "float32")
+    assert_within_steps(out[sel].float().numpy(), ref, torch.float16, abs_sum=bound)
+
+
+def test_addmm_row_shard():
+    m, n, k = 1024, 4096, 4096
+    gen = torch.Generator().manual_seed(4)
+    inp = (torch.randn((m, n), generator=gen)).bfloat16()
+    a = (torch.randn((m, k), generator=gen) * k ** -0.5).bfloat16()
+    b = torch.randn((k, n), generator=gen).bfloat16()
+    out = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    programs.addmm_kernel(inp.to(DEV), a.to(DEV), b.to(DEV), 0.5, 1.5, out)
+    sel = torch.tensor([0, 1, 255, 256, 512, 767, 1023])
+    ref = oracle.addmm(inp[sel], a[sel], b, 0.5, 1.5, "bfloat16")
+    assert_within_steps(out.cpu()[sel].float().numpy(), ref, torch.bfloat16,
+                        abs_sum=addmm_abs_sum(a[sel].float(), b.float(), 1.5))
+
+
+@pytest.mark.parametrize("n_img, c, hw, k", [(8, 256, 56, 256), (4, 256, 56, 256), (2, 256, 32, 320)])
+def test_conv2d_batch_shards(n_img, c, hw, k):
+    # the 8- and 16-GPU image shards of the BASELINE conv and a small batch
+    # with two channel tiles
+    gen = torch.Generator().manual_seed(n_img + c)
+    x = torch.randn((n_img, c, hw, hw), generator=gen).half()
+    w = (torch.randn((k, c, 3, 3), generator=gen) * (2 / (9 * c)) ** 0.5).half()
+    y = programs.conv2d(x.to(DEV), w.to(DEV), padding=1)
+    assert torch.equal(programs.conv2d(x.to(DEV), w.to(DEV), padding=1), y)
+    for sl in (slice(0, 1), slice(n_img - 1, n_img)):
+        ref = oracle.conv2d(x[sl], w, (1, 1), "float16")
+        bound = oracle.conv2d(x[sl].abs(), w.abs(), (1, 1), "float32")
+        assert_within_steps(_np(y[sl]), ref, torch.float16, abs_sum=bound)
+
+
 def test_addmm_512_row_pair_tiles_sampled_rows():
     m, n, k = 4600, 4608, 192
     gen = torch.Generator().manual_seed(11)
