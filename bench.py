@@ -85,6 +85,8 @@ def parse_args():
     p.add_argument("--reference-cpu-path-rows", type=int, default=None, help=argparse.SUPPRESS)
     p.add_argument("--only", default=None, choices=sorted(SINGLE_OPS),
                    help="run W + K launches of one op on its BASELINE shape (for profiling) and exit")
+    p.add_argument("--shard-of", type=int, default=1,
+                   help="with --only: one GPU's shard of the op split over this many GPUs")
     return p.parse_args()
 
 
@@ -663,32 +665,39 @@ def run_single(args):
         return (torch.randn(shape, generator=gen, device=dev) * scale).to(dtype)
 
     op = args.only
+    g = max(1, args.shard_of)  # rank 0's shard of a g-GPU split (sharding.shard_range)
+    rows_l = shard_range(ROWS, 0, g)[1]
+    gemm_l = shard_range(GEMM, 0, g)[1]
+    pairs_l = shard_range(ATT_B * ATT_H, 0, g)[1]
+    imgs_l = shard_range(CONV_N, 0, g)[1]
     if op == "softmax":
-        x = randn(ROWS, COLS, dtype=torch.float16, scale=2.0)
+        x = randn(rows_l, COLS, dtype=torch.float16, scale=2.0)
         y = torch.empty_like(x)
         fn = lambda: programs.softmax_kernel(x, y, BLOCK_SIZE=COLS)  # noqa: E731
-        work, unit = SOFTMAX_BYTES, "GB/s"
+        work, unit = SOFTMAX_BYTES * rows_l / ROWS, "GB/s"
     elif op in ("matmul", "addmm"):
         s = GEMM
-        a, b, c = (randn(s, s, dtype=torch.bfloat16, scale=s ** -0.5) for _ in range(3))
-        out = torch.empty(s, s, device=dev, dtype=torch.bfloat16 if op == "addmm" else torch.float16)
+        a, c = (randn(gemm_l, s, dtype=torch.bfloat16, scale=s ** -0.5) for _ in range(2))
+        b = randn(s, s, dtype=torch.bfloat16, scale=s ** -0.5)
+        out = torch.empty(gemm_l, s, device=dev, dtype=torch.bfloat16 if op == "addmm" else torch.float16)
         if op == "addmm":
             fn = lambda: programs.addmm_kernel(c, a, b, 1.0, 1.0, out)  # noqa: E731
         else:
             fn = lambda: programs.matmul_kernel(a, b, out)  # noqa: E731
-        work, unit = GEMM_FLOPS, "TFLOP/s"
+        work, unit = GEMM_FLOPS * gemm_l / GEMM, "TFLOP/s"
     elif op.startswith("attention"):
         causal = op == "attention_causal"
-        q, k, v = (randn(ATT_B, ATT_H, ATT_S, ATT_D, dtype=torch.bfloat16) for _ in range(3))
+        shape = (ATT_B, ATT_H, ATT_S, ATT_D) if g == 1 else (1, pairs_l, ATT_S, ATT_D)
+        q, k, v = (randn(*shape, dtype=torch.bfloat16) for _ in range(3))
         o = torch.empty_like(q)
         fn = lambda: programs.attention_kernel(q, k, v, causal, o)  # noqa: E731
-        work, unit = ATT_FLOPS / (2 if causal else 1), "TFLOP/s"
+        work, unit = ATT_FLOPS * pairs_l / (ATT_B * ATT_H) / (2 if causal else 1), "TFLOP/s"
     elif op == "conv2d":
-        x = randn(CONV_N, CONV_C, CONV_HW, CONV_HW, dtype=torch.float16)
+        x = randn(imgs_l, CONV_C, CONV_HW, CONV_HW, dtype=torch.float16)
         w = randn(CONV_K, CONV_C, 3, 3, dtype=torch.float16, scale=(2 / (CONV_C * 9)) ** 0.5)
-        y = torch.empty(CONV_N, CONV_K, CONV_HW, CONV_HW, device=dev, dtype=torch.float16)
+        y = torch.empty(imgs_l, CONV_K, CONV_HW, CONV_HW, device=dev, dtype=torch.float16)
         fn = lambda: programs.conv2d_kernel(x, w, y, padding_h=1, padding_w=1)  # noqa: E731
-        work, unit = CONV_FLOPS, "TFLOP/s"
+        work, unit = CONV_FLOPS * imgs_l / CONV_N, "TFLOP/s"
     elif op == "elementwise":
         xa, xb = (randn(ELEMENTS, dtype=torch.float16) for _ in range(2))
         xe = randn(ELEMENTS, dtype=torch.float16, scale=0.5)
@@ -723,7 +732,7 @@ def run_single(args):
     graph = capture_steps(lambda i: fn(), max(args.steps, 1))
     graph_ms = time_graph(graph, torch.cuda.current_stream()) / max(args.steps, 1)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
-    print(json.dumps({"only": op, "ms_eager": ms, "value_eager": work / (ms * 1e-3) / scale, "ms_graph": graph_ms,
+    print(json.dumps({"only": op, "shard_of": g, "ms_eager": ms, "value_eager": work / (ms * 1e-3) / scale, "ms_graph": graph_ms,
                       "value_graph": work / (graph_ms * 1e-3) / scale, "unit": unit,
                       "launches": args.warmup + 3 * args.steps}))
 
