@@ -147,6 +147,47 @@ def test_pow_reference_case_and_golden():
     np.testing.assert_allclose(_np(out), g["output"], rtol=1e-6)
 
 
+def _same_half_bits(got, expected):
+    """Equal bit patterns, NaN counted equal to NaN whatever its payload."""
+    nan = torch.isnan(expected)
+    return bool(torch.equal(torch.isnan(got), nan)) and bool(
+        torch.equal(got.view(torch.int16)[~nan], expected.view(torch.int16)[~nan])
+    )
+
+
+def test_pow_fp16_every_pair_equals_the_fp32_path():
+    # all 2^32 pairs of float16 bit patterns, 256 exponents at a time: the fp16
+    # kernel (table log2, ex2 and the powf fallback near fp16 rounding
+    # boundaries) must give RN_fp16 of the fp32 pow -- torch's and this
+    # library's fp32 kernel -- for every one of them
+    x = torch.arange(0, 1 << 16, dtype=torch.int32, device=DEV).to(torch.int16).view(torch.float16)
+    xs = x.repeat(256)
+    bad = []
+    for y0 in range(0, 1 << 16, 256):
+        ys = torch.arange(y0, y0 + 256, dtype=torch.int32, device=DEV).to(torch.int16).view(torch.float16)
+        ys = ys.repeat_interleave(1 << 16)
+        got = programs.pow(xs, ys)
+        expected = torch.pow(xs.float(), ys.float()).half()
+        if not _same_half_bits(got, expected) or not _same_half_bits(got, programs.pow(xs.float(), ys.float()).half()):
+            bad.append(y0)
+    assert not bad, f"exponent blocks with differing results: {bad[:8]}"
+
+
+def test_pow_fp16_odd_sizes_offsets_and_strides():
+    # the table kernel's vector part and scalar tail (sizes from 2^20 on), the
+    # powf kernel below that, unaligned starts and strided operands: all equal
+    # the fp32 path, on negative bases too
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    n = (1 << 20) + 37
+    base = (torch.randn(n, generator=gen, device=DEV) * 4).half()
+    expo = torch.where(torch.rand(n, generator=gen, device=DEV) < 0.5,
+                       torch.randint(-6, 7, (n,), generator=gen, device=DEV).float(),
+                       torch.randn(n, generator=gen, device=DEV) * 3).half()
+    for a, b in ((base, expo), (base[1:], expo[1:]), (base[::2], expo[::2]), (base[:4099], expo[:4099]),
+                 (base[:13], expo[:13])):
+        assert _same_half_bits(programs.pow(a, b), torch.pow(a.float(), b.float()).half())
+
+
 @pytest.mark.parametrize("name", golden_io.names("dropout_"))
 def test_dropout_golden_bit_exact(name):
     g = golden_io.load(name)
