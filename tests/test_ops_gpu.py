@@ -414,10 +414,11 @@ def test_addmm_row_shard():
                         abs_sum=addmm_abs_sum(a[sel].float(), b.float(), 1.5))
 
 
-@pytest.mark.parametrize("n_img, c, hw, k", [(8, 256, 56, 256), (4, 256, 56, 256), (2, 256, 32, 320)])
+@pytest.mark.parametrize("n_img, c, hw, k", [(8, 256, 56, 256), (4, 256, 56, 256), (2, 256, 32, 320),
+                                              (8, 64, 56, 200), (6, 128, 40, 384)])
 def test_conv2d_batch_shards(n_img, c, hw, k):
-    # the 8- and 16-GPU image shards of the BASELINE conv and a small batch
-    # with two channel tiles
+    # the 8- and 16-GPU image shards of the BASELINE conv, and small batches
+    # with part-filled channel tiles
     gen = torch.Generator().manual_seed(n_img + c)
     x = torch.randn((n_img, c, hw, hw), generator=gen).half()
     w = (torch.randn((k, c, 3, 3), generator=gen) * (2 / (9 * c)) ** 0.5).half()
