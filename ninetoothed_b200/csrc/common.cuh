@@ -103,6 +103,35 @@ inline int launch_status() {
   return static_cast<int>(err);
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_overlapped may
+// be scheduled while the kernel before it in the stream still runs its last
+// CTAs (from the point where every CTA of that kernel has called
+// allow_dependent_launch, or at its end), which hides the launch latency of
+// short back-to-back kernels.  Such a kernel must call wait_prior_grid before
+// it touches global memory: that returns once the previous kernel has
+// completed and its writes are visible, so stream order is kept for any
+// predecessor.  Kernels that follow without the attribute wait as usual.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch_overlapped(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...));
+}
+
 inline bool is_float_dtype(int dtype) {
   return dtype == NT_B200_FLOAT16 || dtype == NT_B200_BFLOAT16 || dtype == NT_B200_FLOAT32;
 }

@@ -65,6 +65,8 @@ rows_in_registers(const T *__restrict__ input, T *__restrict__ output, int64_t r
   constexpr int E = V::N;
   __shared__ float red[32];
   const int64_t nvec = cols / E;
+  wait_prior_grid();
+  allow_dependent_launch();
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const V *src = reinterpret_cast<const V *>(input + row * in_row_stride);
     V *dst = reinterpret_cast<V *>(output + row * out_row_stride);
@@ -173,7 +175,8 @@ template <typename T, int THREADS, int VPT>
 inline void launch_regs(const T *in, T *out, int64_t rows, int64_t cols, int64_t isr, int64_t osr,
                         cudaStream_t stream) {
   const int64_t grid = rows < (1 << 30) ? rows : (1 << 30);
-  rows_in_registers<T, THREADS, VPT><<<(unsigned)grid, THREADS, 0, stream>>>(in, out, rows, cols, isr, osr);
+  launch_overlapped(rows_in_registers<T, THREADS, VPT>, dim3((unsigned)grid), dim3(THREADS), 0, stream, in, out, rows,
+                    cols, isr, osr);
 }
 
 template <typename T>
