@@ -257,6 +257,105 @@ __device__ __forceinline__ void store_accumulator(const Params &prm, uint32_t tm
   }
 }
 
+// Two 16-bit values as one 32-bit word (first in the low half), and back.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_16(float a, float b) {
+  const T x = from_f<T>(a), y = from_f<T>(b);
+  uint16_t ux, uy;
+  memcpy(&ux, &x, 2);
+  memcpy(&uy, &y, 2);
+  return (uint32_t)ux | ((uint32_t)uy << 16);
+}
+template <typename T>
+__device__ __forceinline__ float unpack_16(uint32_t w, int hi) {
+  const uint16_t u = (uint16_t)(hi ? (w >> 16) : (w & 0xffffu));
+  T x;
+  memcpy(&x, &u, 2);
+  return to_f(x);
+}
+
+// store_accumulator for matmul / addmm with a 16-bit, row-contiguous output
+// (and, for addmm, a row-contiguous input) whose rows start on 16-byte
+// boundaries, through a 2 KB shared-memory block per warp: each 32 x 32 chunk
+// is written by rows (a thread holds one row after tcgen05.ld) and read back
+// by row segments, so a warp's global store covers eight rows x 64 contiguous
+// bytes instead of 32 rows x 16 bytes (four times fewer store transactions);
+// addmm's input chunk comes in the same way, transposed.  Slot c of row r
+// sits at 16-byte unit 4 r + ((c + r / 2) mod 4), which keeps both the row
+// and the segment passes free of bank conflicts.  Results are those of
+// store_accumulator.
+template <typename TI, typename TO, Epilogue EPI>
+__device__ __forceinline__ void store_accumulator_staged(const Params &prm, uint32_t tmem_base, uint32_t col0,
+                                                         int quarter, int lane, int64_t row0, int64_t n0,
+                                                         int4 *stage) {
+  static_assert(sizeof(TO) == 2 && (EPI == Epilogue::kMatmul || EPI == Epilogue::kAddmm), "16-bit matmul/addmm");
+  const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16) + col0;
+  const int64_t wrow0 = row0 + quarter * 32;  // this warp's first output row
+  TO *out = static_cast<TO *>(prm.out);
+  const auto unit = [](int r, int c) { return 4 * r + ((c + (r >> 1)) & 3); };
+#pragma unroll 1
+  for (int c = 0; c < 256 / 32; ++c) {
+    uint32_t raw[32];
+    ptx::tmem_ld_32x32b_x32(lane_base + (uint32_t)(c * 32), raw);
+    ptx::tmem_ld_wait();
+    const int64_t nc = n0 + c * 32;
+    if (nc >= prm.N) continue;  // the same in every lane
+    const bool full = prm.N - nc >= 32;
+    const int64_t m = wrow0 + lane;
+    float v[32];
+    if constexpr (EPI == Epilogue::kMatmul) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = round_f16(__uint_as_float(raw[e]));
+    } else {
+      float in_v[32];
+      if (full) {
+        const TI *bias = static_cast<const TI *>(prm.bias) + nc;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // segments: rows 8i .. 8i + 7, four 16-byte slots each
+          const int r = 8 * i + (lane >> 2), slot = lane & 3;
+          const int64_t mr = wrow0 + r;
+          stage[unit(r, slot)] =
+              mr < prm.M ? __ldcs(reinterpret_cast<const int4 *>(bias + mr * prm.sim) + slot) : make_int4(0, 0, 0, 0);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int4 q = stage[unit(lane, j)];
+          const uint32_t w[4] = {(uint32_t)q.x, (uint32_t)q.y, (uint32_t)q.z, (uint32_t)q.w};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) in_v[j * 8 + e] = unpack_16<TI>(w[e >> 1], e & 1);
+        }
+        __syncwarp();
+      } else {
+        const int valid = (int)(prm.N - nc);
+        const TI *bias = static_cast<const TI *>(prm.bias) + m * prm.sim + nc * prm.sin;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) in_v[e] = (e < valid && m < prm.M) ? to_f(bias[e * prm.sin]) : 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < 32; ++e) v[e] = addmm_value<TI>(prm.beta, prm.alpha, in_v[e], __uint_as_float(raw[e]));
+    }
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        stage[unit(lane, j)] =
+            make_int4((int)pack2_16<TO>(v[j * 8 + 0], v[j * 8 + 1]), (int)pack2_16<TO>(v[j * 8 + 2], v[j * 8 + 3]),
+                      (int)pack2_16<TO>(v[j * 8 + 4], v[j * 8 + 5]), (int)pack2_16<TO>(v[j * 8 + 6], v[j * 8 + 7]));
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + (lane >> 2), slot = lane & 3;
+        const int64_t mr = wrow0 + r;
+        if (mr < prm.M) *(reinterpret_cast<int4 *>(out + mr * prm.som + nc) + slot) = stage[unit(r, slot)];
+      }
+      __syncwarp();
+    } else if (m < prm.M) {
+      const int valid = (int)(prm.N - nc);
+      for (int e = 0; e < valid; ++e) out[m * prm.som + (nc + e) * prm.son] = from_f<TO>(v[e]);
+    }
+  }
+}
+
 template <typename TI, typename TO, Epilogue EPI, bool B_MN_MAJOR>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, Params prm) {
@@ -460,7 +559,11 @@ struct PairCfg {
   static constexpr int A_STAGE_BYTES = MB * BM * 128;
   static constexpr int NBUF = MB == 1 ? 2 : 1;  // accumulator sets of MB x BN columns
   static constexpr int GROUP_M = 16 / MB;       // raster groups of 4096 A rows
-  static constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + CTRL_BYTES;
+  // MB = 2: a 2 KB output staging block per epilogue warp after the control
+  // block (store_accumulator_staged)
+  static constexpr int EPI_STAGE_BYTES = MB == 2 ? 8 * 2048 : 0;
+  static constexpr int SMEM_BYTES =
+      STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 1024 /*align*/ + CTRL_BYTES + EPI_STAGE_BYTES;
   static_assert(NBUF * MB * BN <= TMEM_COLS, "TMEM columns");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
 };
@@ -816,6 +919,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     const int h = (warp - 2) >> 2;  // A block whose accumulator this warp drains
+    // row-contiguous 16-byte-aligned rows: the output (and addmm's input) go
+    // through the warp's shared-memory staging block
+    const auto aligned16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+    bool staged_epilogue = prm.son == 1 && prm.som % 8 == 0 && aligned16(prm.out);
+    if constexpr (EPI == Epilogue::kAddmm)
+      staged_epilogue = staged_epilogue && prm.sin == 1 && prm.sim % 8 == 0 && aligned16(prm.bias);
+    (void)staged_epilogue;
     int local = 0;
     for (int tile = pair; tile < num_tiles; tile += pairs, ++local) {
       const int buf = local % NBUF;
@@ -824,13 +934,25 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       ptx::tc_fence_after();
       int mb, nb;
       gemm::tile_coords(tile, prm.tiles_m, prm.tiles_n, mb, nb, GROUP);
-      if constexpr (is_conv(EPI))
+      if constexpr (is_conv(EPI)) {
         gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)(buf * BN), quarter, lane,
                                              (int64_t)(mb % prm.conv_tiles_img) * (2 * BM) + rank * BM,
                                              (int64_t)nb * BN, mb / prm.conv_tiles_img);
-      else
-        gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)((buf * MB + h) * BN), quarter, lane,
-                                             (int64_t)mb * TILE_M + rank * (MB * BM) + h * BM, (int64_t)nb * BN, 0);
+      } else {
+        const int64_t row0 = (int64_t)mb * TILE_M + rank * (MB * BM) + h * BM;
+        bool done = false;
+        if constexpr (MB == 2 && sizeof(TO) == 2) {
+          if (staged_epilogue) {
+            int4 *stage = reinterpret_cast<int4 *>(ctrl + CTRL_BYTES + (warp - 2) * 2048);
+            gemm::store_accumulator_staged<TI, TO, EPI>(prm, tmem_base, (uint32_t)((buf * MB + h) * BN), quarter, lane,
+                                                        row0, (int64_t)nb * BN, stage);
+            done = true;
+          }
+        }
+        if (!done)
+          gemm::store_accumulator<TI, TO, EPI>(prm, tmem_base, (uint32_t)((buf * MB + h) * BN), quarter, lane, row0,
+                                               (int64_t)nb * BN, 0);
+      }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa(tempty_bar(buf), 0));
