@@ -113,6 +113,83 @@ rows_in_registers(const T *__restrict__ input, T *__restrict__ output, int64_t r
   }
 }
 
+// rows_in_registers for a grid of at most the resident CTAs, each taking
+// several rows: a CTA loads its next row while it reduces and writes the
+// current one (the same arithmetic, so the same results).
+template <typename T, int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS)
+rows_prefetched(const T *__restrict__ input, T *__restrict__ output, int64_t rows, int64_t cols,
+                int64_t in_row_stride, int64_t out_row_stride) {
+  using V = Vec<T>;
+  constexpr int E = V::N;
+  __shared__ float red[32];
+  const int64_t nvec = cols / E;
+  wait_prior_grid();
+  allow_dependent_launch();
+  int4 raw[VPT];
+  int64_t row = blockIdx.x;
+  if (row < rows) {
+    const V *src = reinterpret_cast<const V *>(input + row * in_row_stride);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t idx = (int64_t)j * THREADS + threadIdx.x;
+      raw[j] = idx < nvec ? __ldcs(reinterpret_cast<const int4 *>(src + idx)) : make_int4(0, 0, 0, 0);
+    }
+  }
+  for (; row < rows; row += gridDim.x) {
+    V *dst = reinterpret_cast<V *>(output + row * out_row_stride);
+    float x[VPT][E];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t idx = (int64_t)j * THREADS + threadIdx.x;
+      if (idx < nvec) {
+        V vec;
+        *reinterpret_cast<int4 *>(&vec) = raw[j];
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          x[j][e] = to_f(vec.v[e]);
+          m = fmaxf(m, x[j][e]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[j][e] = -INFINITY;
+      }
+    }
+    const int64_t next = row + gridDim.x;
+    if (next < rows) {
+      const V *src = reinterpret_cast<const V *>(input + next * in_row_stride);
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int64_t idx = (int64_t)j * THREADS + threadIdx.x;
+        raw[j] = idx < nvec ? __ldcs(reinterpret_cast<const int4 *>(src + idx)) : make_int4(0, 0, 0, 0);
+      }
+    }
+    m = block_reduce_max<THREADS>(m, red);
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        x[j][e] = fast_exp<T>(x[j][e] - m);
+        s += x[j][e];
+      }
+    }
+    s = block_reduce_sum<THREADS>(s, red);
+    const float inv = 1.f / s;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int64_t idx = (int64_t)j * THREADS + threadIdx.x;
+      if (idx < nvec) {
+        V vec;
+#pragma unroll
+        for (int e = 0; e < E; ++e) vec.v[e] = from_f<T>(x[j][e] * inv);
+        __stcs(reinterpret_cast<int4 *>(dst + idx), *reinterpret_cast<int4 *>(&vec));
+      }
+    }
+  }
+}
+
 // Unit column stride, any row length and alignment: the row in registers as
 // EPT scalars per thread (element j * THREADS + t), loaded and stored with
 // coalesced scalar accesses, so a row is still read from HBM once.
@@ -174,9 +251,33 @@ rows_strided(const T *__restrict__ input, T *__restrict__ output, int64_t rows, 
 template <typename T, int THREADS, int VPT>
 inline void launch_regs(const T *in, T *out, int64_t rows, int64_t cols, int64_t isr, int64_t osr,
                         cudaStream_t stream) {
-  const int64_t grid = rows < (1 << 30) ? rows : (1 << 30);
-  launch_overlapped(rows_in_registers<T, THREADS, VPT>, dim3((unsigned)grid), dim3(THREADS), 0, stream, in, out, rows,
-                    cols, isr, osr);
+  // Up to four rows per resident CTA (such as one GPU's shard of a split
+  // batch): a grid of at most the CTAs that fit on the GPU at once (per
+  // device, found on first use), each prefetching its next row.  More rows:
+  // one CTA per row.
+  static std::atomic<int> resident[64] = {};
+  int device = 0;
+  cudaGetDevice(&device);
+  int per_sm = (device >= 0 && device < 64) ? resident[device].load(std::memory_order_relaxed) : 0;
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_prefetched<T, THREADS, VPT>, THREADS,
+                                                      0) != cudaSuccess ||
+        per_sm <= 0) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    if (device >= 0 && device < 64) resident[device].store(per_sm, std::memory_order_relaxed);
+  }
+  const int64_t cap = (int64_t)per_sm * sm_count();
+  if (rows <= 4 * cap) {
+    const int64_t grid = rows < cap ? rows : cap;
+    launch_overlapped(rows_prefetched<T, THREADS, VPT>, dim3((unsigned)grid), dim3(THREADS), 0, stream, in,
+                      out, rows, cols, isr, osr);
+  } else {
+    const int64_t grid = rows < (1 << 30) ? rows : (1 << 30);
+    launch_overlapped(rows_in_registers<T, THREADS, VPT>, dim3((unsigned)grid), dim3(THREADS), 0, stream, in,
+                      out, rows, cols, isr, osr);
+  }
 }
 
 template <typename T>

@@ -77,11 +77,13 @@ def test_softmax_baseline_config(dtype):
     assert torch.allclose(y.float().sum(-1), torch.ones(16384, device=DEV), atol=1e-2)
 
 
-@pytest.mark.parametrize("rows, cols", [(1, 4096), (7, 2048), (900, 1032), (5000, 4096), (3000, 3000), (4441, 4104)])
+@pytest.mark.parametrize("rows, cols", [(1, 4096), (7, 2048), (900, 1032), (2048, 4096), (2500, 4096), (5000, 4096),
+                                       (3000, 3000), (4441, 4104)])
 @pytest.mark.parametrize("dtype", (torch.float16, torch.bfloat16))
 def test_softmax_rows_of_many_lengths(rows, cols, dtype):
-    # rows of 129-513 vectors: fewer and more rows than resident CTAs, row
-    # lengths on and off the 16-byte vector grid (3000: the scalar path)
+    # rows of 129-513 vectors: fewer and more rows than resident CTAs (up to
+    # four rows a resident CTA: the prefetching kernel), row lengths on and
+    # off the 16-byte vector grid (3000: the scalar path)
     gen = torch.Generator().manual_seed(rows + cols)
     x = (torch.randn(rows, cols, generator=gen) * 2).to(dtype)
     y = programs.softmax(x.to(DEV))
