@@ -137,6 +137,7 @@ constexpr int kPowQueue = 64;  // deferred elements per warp
 struct PowHalfShared {
   float log2_abs[32768];                          // log2 of |x| by fp16 bit pattern
   int64_t queue[kPowThreads / 32][kPowQueue];     // deferred element indices per warp
+  int fill[kPowThreads / 32];                     // places taken in a warp's queue this step
 };
 
 __device__ __forceinline__ void build_pow_table(PowHalfShared &sh) {
@@ -164,6 +165,7 @@ __device__ __forceinline__ void build_pow_table(PowHalfShared &sh) {
     }
     sh.log2_abs[xb] = v;
   }
+  if (threadIdx.x < kPowThreads / 32) sh.fill[threadIdx.x] = 0;
   __syncthreads();  // the fraction table's space becomes the queues
 }
 
@@ -245,40 +247,44 @@ pow_half_kernel(const __half *__restrict__ a, const __half *__restrict__ b, __ha
       for (int e = 0; e < V::N; e += 2) *reinterpret_cast<__half2 *>(&z.v[e]) = __floats2half2_rn(r[e], r[e + 1]);
       __stcs(reinterpret_cast<int4 *>(vo + idx[h]), *reinterpret_cast<int4 *>(&z));
     }
-    // queue this step's slow elements; compute 32 of them once 32 are queued
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t bits = slow[h];
-      if (!__ballot_sync(0xffffffffu, bits != 0)) continue;
-      const int n = __popc(bits);
-      int incl = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const int total = __shfl_sync(0xffffffffu, incl, 31);
+    // queue this step's slow elements (lanes take consecutive places from
+    // the warp's fill counter, in any order); compute 32 of them once 32 are
+    // queued
+    const int n = __popc(slow[0]) + __popc(slow[1]);
+    const int total = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
+    if (total != 0) {
       if (count + total > kPowQueue) {  // no room: compute what is queued first
         for (int q = lane; q < count; q += 32) pow_half_slow(a, b, out, queue[q]);
         count = 0;
         __syncwarp();
       }
       if (total > kPowQueue) {  // more than a queue's worth: every lane its own
-        while (bits) {
-          const int e = __ffs(bits) - 1;
-          bits &= bits - 1;
-          pow_half_slow(a, b, out, idx[h] * V::N + e);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t bits = slow[h];
+          while (bits) {
+            const int e = __ffs(bits) - 1;
+            bits &= bits - 1;
+            pow_half_slow(a, b, out, idx[h] * V::N + e);
+          }
         }
       } else {
-        int pos = count + incl - n;
-        while (bits) {
-          const int e = __ffs(bits) - 1;
-          bits &= bits - 1;
-          queue[pos++] = idx[h] * V::N + e;
+        int pos = count;
+        if (n != 0) pos += atomicAdd(&sh.fill[warp], n);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t bits = slow[h];
+          while (bits) {
+            const int e = __ffs(bits) - 1;
+            bits &= bits - 1;
+            queue[pos++] = idx[h] * V::N + e;
+          }
         }
-        count += total;
         __syncwarp();  // queue entries and this step's vector stores ordered before the powf pass
-        if (count >= 32) {
+        if (lane == 0) sh.fill[warp] = 0;
+        count += total;
+        __syncwarp();
+        while (count >= 32) {
           pow_half_slow(a, b, out, queue[count - 32 + lane]);
           count -= 32;
           __syncwarp();
