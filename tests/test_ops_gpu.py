@@ -686,6 +686,17 @@ def test_softmax_host_streaming_matches_device_softmax(rows, cols, chunks):
     again = programs.softmax_host(x, out, chunks=chunks)  # reuse of the output buffer
     torch.cuda.current_stream().synchronize()
     assert again is out and torch.equal(out, expected)
+    # pageable output: the GPU cannot write it, so each chunk is copied back
+    pageable = torch.full_like(x, float("nan"))
+    assert not pageable.is_pinned()
+    programs.softmax_host(x, pageable, chunks=chunks)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(pageable, expected)
+    # default chunking
+    out.fill_(float("nan"))
+    programs.softmax_host(x, out)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out, expected)
 
 
 @pytest.mark.parametrize("inside", [False, True], ids=["two_kernels", "pool_in_conv_kernel"])
