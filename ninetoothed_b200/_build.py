@@ -25,6 +25,12 @@ NVCC_FLAGS = (
     "-std=c++17",
     "-Xcompiler",
     "-fPIC",
+    # function-local statics of templates (the per-device shared-memory
+    # opt-in and occupancy caches) stay private to this library: as GNU
+    # "unique" symbols a second build loaded into the same process would share
+    # them and launch its kernels without their shared-memory opt-in
+    "-Xcompiler",
+    "-fno-gnu-unique",
     "-shared",
 )
 

@@ -801,6 +801,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   ptx::cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_base_ptr;
+  // launched as a programmatic dependent of the kernel before it in the
+  // stream (the conv's staging pass, the previous GEMM): the set-up above ran
+  // beside that kernel's last CTAs; global memory is touched only from here,
+  // once its writes are visible
+  wait_prior_grid();
+  allow_dependent_launch();
 
   const int num_tiles = prm.tiles_m * prm.tiles_n;
   const int num_kb = prm.num_kb;
@@ -1017,8 +1023,9 @@ int launch_pair(const CUtensorMap &ta, const CUtensorMap &tb, const gemm::Params
   }
   const int64_t tiles = (int64_t)prm.tiles_m * prm.tiles_n;
   const int grid_pairs = (int)(tiles < pairs ? tiles : pairs);
-  kern<<<2 * grid_pairs, threads, smem, stream>>>(ta, tb, prm);
-  return launch_status();
+  const int launched = launch_overlapped(kern, dim3(2 * (unsigned)grid_pairs), dim3(threads), smem, stream, ta, tb, prm);
+  const int st = launch_status();
+  return launched != 0 ? launched : st;
 }
 
 // Launches the tensor-core GEMM when the operands meet its layout rules;
@@ -1148,6 +1155,7 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 nchw_to_nhwc_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int wp, int pad_w,
                     int64_t isn, int64_t isc, int64_t ish, int64_t isw, FilterStaging<T> filter) {
+  allow_dependent_launch();  // the conv GEMM waits for this grid's writes
   if (blockIdx.z == 0) {
     stage_filter(filter, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     return;
@@ -1185,6 +1193,7 @@ __global__ void __launch_bounds__(256)
 nchw_to_nhwc_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int HW, int W, int wp, int pad_w,
                         int64_t isn, int64_t isc, FilterStaging<T> filter) {
   static_assert(sizeof(T) == 2, "16-bit elements");
+  allow_dependent_launch();  // the conv GEMM waits for this grid's writes
   if (blockIdx.z == 0) {
     stage_filter(filter, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
     return;
