@@ -83,6 +83,8 @@ __global__ void binary_vec(const T *__restrict__ a, const T *__restrict__ b, T *
   const V *va = reinterpret_cast<const V *>(a);
   const V *vb = reinterpret_cast<const V *>(b);
   V *vo = reinterpret_cast<V *>(out);
+  wait_prior_grid();  // launched as a programmatic dependent (launch_overlapped)
+  allow_dependent_launch();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
     V x, y, z;
@@ -206,7 +208,9 @@ pow_half_kernel(const __half *__restrict__ a, const __half *__restrict__ b, __ha
                 int64_t nvec) {
   extern __shared__ __align__(16) uint8_t pow_smem[];
   PowHalfShared &sh = *reinterpret_cast<PowHalfShared *>(pow_smem);
-  build_pow_table(sh);
+  build_pow_table(sh);  // no global memory: runs beside the previous kernel's tail
+  wait_prior_grid();    // launched as a programmatic dependent (launch_overlapped)
+  allow_dependent_launch();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int64_t *queue = sh.queue[warp];
   using V = Vec<__half>;
@@ -303,6 +307,8 @@ __global__ void dropout_vec(const T *__restrict__ in, T *__restrict__ out, int64
   V *vo = reinterpret_cast<V *>(out);
   const float keep = 1.f - p;
   const float inv_keep = __frcp_rn(keep);
+  wait_prior_grid();  // launched as a programmatic dependent (launch_overlapped)
+  allow_dependent_launch();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec;
        i += (int64_t)gridDim.x * blockDim.x) {
     V x, z;
@@ -352,7 +358,11 @@ int run_binary(const void *a, const void *b, void *out, int64_t size, int64_t sa
   int64_t done = 0;
   if (sa == 1 && sb == 1 && so == 1 && vec_ok<T>(a) && vec_ok<T>(b) && vec_ok<T>(out)) {
     const int64_t nvec = size / Vec<T>::N;
-    if (nvec > 0) binary_vec<T, Op><<<grid_for(nvec, THREADS), THREADS, 0, stream>>>(pa, pb, po, nvec, op);
+    if (nvec > 0) {
+      const int e = launch_overlapped(binary_vec<T, Op>, dim3(grid_for(nvec, THREADS)), dim3(THREADS), 0, stream, pa,
+                                      pb, po, nvec, op);
+      if (e != 0) return launch_status();  // the launch's error, cleared
+    }
     done = nvec * Vec<T>::N;
   }
   if (done < size)
@@ -377,7 +387,9 @@ int run_pow(const void *a, const void *b, void *out, int64_t size, int64_t sa, i
       const int64_t nvec = size / Vec<T>::N;
       const cudaError_t e = smem_optin<pow_half_kernel>((int)sizeof(PowHalfShared));
       if (e != cudaSuccess) return (int)e;
-      pow_half_kernel<<<sm_count(), kPowThreads, sizeof(PowHalfShared), stream>>>(pa, pb, po, nvec);
+      const int le = launch_overlapped(pow_half_kernel, dim3(sm_count()), dim3(kPowThreads), sizeof(PowHalfShared),
+                                       stream, pa, pb, po, nvec);
+      if (le != 0) return launch_status();  // the launch's error, cleared
       const int64_t done = nvec * Vec<T>::N;
       if (done < size)
         binary_strided<T, PowOp><<<grid_for(size - done, THREADS), THREADS, 0, stream>>>(pa, pb, po, size, 1, 1, 1,
@@ -401,8 +413,11 @@ int run_dropout(const void *in, void *out, int64_t size, int64_t si, int64_t so,
   int64_t done = 0;
   if (si == 1 && so == 1 && vec_ok<T>(in) && vec_ok<T>(out)) {
     const int64_t nvec = size / Vec<T>::N;
-    if (nvec > 0)
-      dropout_vec<T><<<grid_for(nvec, THREADS), THREADS, 0, stream>>>(pi, po, nvec, p, key_lo, key_hi);
+    if (nvec > 0) {
+      const int e = launch_overlapped(dropout_vec<T>, dim3(grid_for(nvec, THREADS)), dim3(THREADS), 0, stream, pi, po,
+                                      nvec, p, key_lo, key_hi);
+      if (e != 0) return launch_status();  // the launch's error, cleared
+    }
     done = nvec * Vec<T>::N;
   }
   if (done < size)

@@ -227,6 +227,10 @@ __global__ void __launch_bounds__(256)
 max_pool2d_3x3s2p1_vec_kernel(const T *__restrict__ in, T *__restrict__ out, int C, int H, int W, int P, int Q,
                               int64_t isn, int64_t isc, int64_t ish, int64_t osn, int64_t osc, int64_t osp,
                               int pairs_per_plane, int64_t total_pairs) {
+  // launched as a programmatic dependent (launch_overlapped); no early
+  // trigger for the next kernel: this grid runs several waves, and dependents
+  // let in from its last wave on made it slower
+  wait_prior_grid();
   const int lane = threadIdx.x & 31;
   const int j = lane & 7;  // lane within the group
   const int64_t g = (int64_t)blockIdx.x * 32 + (threadIdx.x >> 3);
@@ -282,9 +286,9 @@ inline void launch_vec(const T *in, T *out, int64_t n, int64_t c, int64_t h, int
     const int pairs_per_plane = (int)((P + 1) / 2);
     const int64_t total_pairs = n * c * pairs_per_plane;
     const int64_t blocks = (total_pairs + 31) / 32;
-    max_pool2d_3x3s2p1_vec_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(
-        in, out, (int)c, (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], pairs_per_plane,
-        total_pairs);
+    launch_overlapped(max_pool2d_3x3s2p1_vec_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, stream, in, out, (int)c,
+                      (int)h, (int)w, (int)P, (int)Q, is[0], is[1], is[2], os[0], os[1], os[2], pairs_per_plane,
+                      total_pairs);  // a failed launch is read by the caller's launch_status()
   }
 }
 
