@@ -806,7 +806,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   // beside that kernel's last CTAs; global memory is touched only from here,
   // once its writes are visible
   wait_prior_grid();
-  allow_dependent_launch();
 
   const int num_tiles = prm.tiles_m * prm.tiles_n;
   const int num_kb = prm.num_kb;
@@ -872,6 +871,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
+      // this CTA's last loads are issued: the next kernel may be scheduled
+      // (triggered earlier, a dependent's waiting CTAs sat beside the whole
+      // GEMM and slowed it, e.g. the max_pool2d after a conv)
+      allow_dependent_launch();
       // Wait until the MMAs have released every stage this CTA filled, so that
       // no commit arrival is still in flight towards this CTA when it exits.
       for (int i = 0; i < STAGES && ok; ++i) {
