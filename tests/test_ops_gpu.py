@@ -734,3 +734,36 @@ def test_conv2d_max_pool2d_equals_the_two_programs(nchw, k, rs, pad, dtype, insi
     pooled_tol = oracle.max_pool2d(tol, (3, 3), out_hw, stride=(2, 2), padding=(1, 1))
     err = np.abs(_np(fused) - pooled_ref)
     assert (err <= pooled_tol).all(), f"max err {err.max()}"
+
+
+@pytest.mark.gpu
+def test_dependent_launches_read_their_predecessors_output():
+    # add, the fp16 pow, dropout, max_pool2d, softmax and the CTA-pair GEMM
+    # are launched as programmatic dependents of the kernel before them; each
+    # must wait for that kernel's writes.  Chains whose every step reads the
+    # step before, queued back to back, equal the same steps synchronised one
+    # by one.
+    gen = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(1 << 24, device=DEV, generator=gen).half()
+    e = (torch.rand(1 << 24, device=DEV, generator=gen) * 3).half()
+    a = (torch.randn(2048, 4096, device=DEV, generator=gen) * 4096 ** -0.5).bfloat16()
+    b = (torch.randn(4096, 4096, device=DEV, generator=gen) * 4096 ** -0.5).bfloat16()
+    img = torch.randn(8, 256, 56, 56, device=DEV, generator=gen).half()
+    flt = (torch.randn(256, 256, 3, 3, device=DEV, generator=gen) * 0.05).half()
+
+    def chains(sync):
+        step = torch.cuda.synchronize if sync else (lambda: None)
+        y = programs.add(x, x); step()
+        y = programs.pow(y.abs(), e); step()
+        y = programs.dropout(y, p=0.25, seed=5); step()
+        c = programs.matmul(a, b); step()
+        c = programs.matmul(c.bfloat16(), b); step()
+        s = programs.softmax(c); step()
+        f = programs.conv2d(img, flt, padding=1); step()
+        p = programs.max_pool2d(f, (3, 3), stride=(2, 2), padding=(1, 1)); step()
+        torch.cuda.synchronize()
+        return y, c, s, p
+
+    for queued, stepped in zip(chains(False), chains(True)):
+        assert torch.equal(queued, stepped)
+    assert device_status() == 0
