@@ -121,6 +121,8 @@ def softmax_config(world):
     return {
         "workload": "row softmax fp16 [16384, 4096] (BASELINE configs[1]), one pass over the whole tensor per step",
         "rows": ROWS, "cols": COLS,
+        "l2": "inputs larger than L2, no flush: the GPU arm rotates input/output buffers of at least 1 GiB "
+              "a rank (> 126 MB L2) between timed launches",
     }
 
 
