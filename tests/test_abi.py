@@ -72,3 +72,24 @@ def test_empty_launches_are_no_ops():
     assert lib.nt_b200_softmax(None, None, 0, 4, 4, 1, 4, 1, 8, None) == 0
     assert lib.nt_b200_add(None, None, None, 0, 1, 1, 1, 10, None) == 0
     assert lib.nt_b200_matmul(None, None, None, 0, 4, 4, 4, 1, 4, 1, 4, 1, 8, 8, None) == 0
+
+
+def test_library_keeps_its_per_device_caches_private():
+    # Function-local statics of templates (per-device shared-memory opt-in,
+    # resident CTA pairs) must not become GNU "unique" symbols: those are
+    # shared process-wide, so a second build loaded beside this one would
+    # skip its own kernels' shared-memory opt-in and fail to launch them.
+    import shutil
+    import subprocess
+
+    from ninetoothed_b200 import _build
+
+    assert "-fno-gnu-unique" in _build.NVCC_FLAGS
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm is not installed")
+    _lib.library()  # built if missing
+    table = subprocess.run([nm, "-D", "--defined-only", str(_build.LIBRARY)], capture_output=True, text=True,
+                           check=True).stdout
+    unique = [line for line in table.splitlines() if line.split()[-2:-1] == ["u"]]
+    assert unique == [], unique[:5]
