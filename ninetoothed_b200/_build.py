@@ -47,10 +47,12 @@ def find_nvcc() -> str:
 
 
 def sources() -> list[Path]:
+    """Files the library depends on, this one included (its compiler flags)."""
     return sorted(
         list(SOURCE_DIR.glob("*.cu"))
         + list(SOURCE_DIR.glob("*.cuh"))
         + list(INCLUDE_DIR.glob("*.h"))
+        + [Path(__file__).resolve()]
     )
 
 
